@@ -1,0 +1,349 @@
+// Host side of the tcgen05 W4A8 GEMM and implicit-GEMM convolution:
+// argument checks, tile/pipeline sizing, TMA tensor maps, launch.
+#include <algorithm>
+
+#include "mma_kernel.cuh"
+#include "tensormap.cuh"
+
+namespace w4a8 {
+
+__device__ unsigned g_device_error;
+
+unsigned* device_error_word() {
+  static unsigned* cached[64] = {nullptr};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  void* ptr = nullptr;
+  if (cudaGetSymbolAddress(&ptr, g_device_error) != cudaSuccess) return nullptr;
+  if (dev >= 0 && dev < 64) cached[dev] = static_cast<unsigned*>(ptr);
+  return static_cast<unsigned*>(ptr);
+}
+
+namespace {
+
+constexpr int kSmemAttr = 226 * 1024;         // dynamic smem requested per CTA
+constexpr int kSmemBudget = kSmemAttr - 1024;  // minus base-alignment slack
+
+template <int BN, bool I4, bool CV>
+int launch_t(const CUtensorMap& tA, const CUtensorMap& tW, const CUtensorMap* tH, const KParams& p, int grid,
+             cudaStream_t st) {
+  auto kern = w4a8_mma_kernel<BN, I4, CV>;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAttr) != cudaSuccess)
+      return W4A8_ERR_LAUNCH;
+    if (dev >= 0 && dev < 64) attr_done[dev] = true;
+  }
+  kern<<<grid, kThreads, kSmemAttr, st>>>(tA, tW, tH[0], tH[1], tH[2], tH[3], p);
+  return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH;
+}
+
+template <bool I4, bool CV>
+int launch_bn(int bn, const CUtensorMap& tA, const CUtensorMap& tW, const CUtensorMap* tH, const KParams& p,
+              int grid, cudaStream_t st) {
+  switch (bn) {
+    case 64: return launch_t<64, I4, CV>(tA, tW, tH, p, grid, st);
+    case 128: return launch_t<128, I4, CV>(tA, tW, tH, p, grid, st);
+    case 256: return launch_t<256, I4, CV>(tA, tW, tH, p, grid, st);
+    default: return W4A8_ERR_UNSUPPORTED;
+  }
+}
+
+int launch(bool i4, bool cv, int bn, const CUtensorMap& tA, const CUtensorMap& tW, const CUtensorMap* tH,
+           const KParams& p, int grid, cudaStream_t st) {
+  if (i4) return cv ? launch_bn<true, true>(bn, tA, tW, tH, p, grid, st)
+                    : launch_bn<true, false>(bn, tA, tW, tH, p, grid, st);
+  return cv ? launch_bn<false, true>(bn, tA, tW, tH, p, grid, st)
+            : launch_bn<false, false>(bn, tA, tW, tH, p, grid, st);
+}
+
+int check_epilogue(const w4a8_epilogue* e) {
+  if (!e) return W4A8_ERR_ARG;
+  if (e->out_kind < W4A8_OUT_S32 || e->out_kind > W4A8_OUT_S8) return W4A8_ERR_ARG;
+  if (e->out_kind == W4A8_OUT_S8) {
+    if (!(e->out_scale > 0.0f)) return W4A8_ERR_ARG;
+    if (e->qn < -128 || e->qp > 127 || e->qn > e->qp) return W4A8_ERR_ARG;
+  }
+  return W4A8_OK;
+}
+
+void fill_epi(EpiParams& d, const w4a8_epilogue* e, void* out, int n_total) {
+  d.out = out;
+  d.out_kind = e->out_kind;
+  d.relu = e->relu;
+  d.alpha = e->alpha;
+  d.alpha_scalar = e->alpha_scalar;
+  d.beta = e->beta;
+  d.residual = e->residual;
+  d.res_ld = e->res_ld;
+  d.out_scale = e->out_scale;
+  d.qn = e->qn;
+  d.qp = e->qp;
+  d.aux = e->aux;
+  d.aux_ld = e->aux_ld;
+  d.n_total = n_total;
+}
+
+int pick_stages(uint32_t per_stage, uint32_t reserved) {
+  if (reserved + 2 * per_stage > static_cast<uint32_t>(kSmemBudget)) return 0;
+  return std::min<int>(kMaxStages, (kSmemBudget - reserved) / per_stage);
+}
+
+int floordiv(int a, int b) { return a >= 0 ? a / b : -((-a + b - 1) / b); }
+
+}  // namespace
+}  // namespace w4a8
+
+using namespace w4a8;
+
+extern "C" int w4a8_abi_version(void) { return W4A8_ABI_VERSION; }
+extern "C" int w4a8_num_sms(void) { return device_sms(); }
+
+extern "C" int w4a8_device_error(unsigned* bits) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return W4A8_ERR_LAUNCH;
+  unsigned* word = device_error_word();
+  if (!word) return W4A8_ERR_LAUNCH;
+  unsigned v = 0;
+  if (cudaMemcpy(&v, word, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return W4A8_ERR_LAUNCH;
+  if (bits) *bits = v;
+  if (v) {
+    const unsigned zero = 0;
+    cudaMemcpy(word, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+    return W4A8_ERR_DEVICE;
+  }
+  return W4A8_OK;
+}
+
+extern "C" int w4a8_gemm(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int w_kind, int M, int N,
+                         int K, const w4a8_epilogue* epi, void* C, int64_t ldc, void* stream) {
+  if (M < 0 || N < 0 || K <= 0) return W4A8_ERR_ARG;
+  if (w_kind != W4A8_W_INT8 && w_kind != W4A8_W_INT4) return W4A8_ERR_ARG;
+  const bool i4 = w_kind == W4A8_W_INT4;
+  if (i4 && (K & 1)) return W4A8_ERR_ARG;
+  if (int rc = check_epilogue(epi)) return rc;
+  if (M == 0 || N == 0) return W4A8_OK;
+  if (!A || !W || !C) return W4A8_ERR_ARG;
+  if (lda < K || ldw < (i4 ? K / 2 : K) || ldc < N) return W4A8_ERR_ARG;
+  if ((lda % 16) || (ldw % 16) || !aligned16(A) || !aligned16(W)) return W4A8_ERR_ALIGN;
+
+  const int sms = device_sms();
+  const int tiles_m = (M + kBM - 1) / kBM;
+  int bn = N > 128 ? 256 : (N > 64 ? 128 : 64);
+  while (bn > 64 && tiles_m * ((N + bn - 1) / bn) < sms) bn >>= 1;
+
+  KParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = M;
+  p.N = N;
+  p.num_kb = (K + kBK - 1) / kBK;
+  p.tiles_m = tiles_m;
+  p.tiles_n = (N + bn - 1) / bn;
+  p.a_stage_bytes = kBM * kBK;
+  p.b_stage_bytes = bn * kBK;
+  p.bp_stage_bytes = i4 ? bn * kBK / 2 : 0;
+  const uint32_t per_stage = p.a_stage_bytes + p.b_stage_bytes + p.bp_stage_bytes;
+  p.stages = pick_stages(per_stage, 0);
+  if (p.stages < 2) return W4A8_ERR_UNSUPPORTED;
+  p.halo_stages = 0;
+  p.a_off = 0;
+  p.b_off = p.a_off + p.stages * p.a_stage_bytes;
+  p.bp_off = p.b_off + p.stages * p.b_stage_bytes;
+  p.h_off = p.bp_off + p.stages * p.bp_stage_bytes;
+  p.tx_bytes = p.a_stage_bytes + (i4 ? p.bp_stage_bytes : p.b_stage_bytes);
+  p.tmem_cols = 2 * bn < 32 ? 32 : 2 * bn;
+  p.err = device_error_word();
+  if (!p.err) return W4A8_ERR_LAUNCH;
+  fill_epi(p.epi, epi, C, N);
+  p.epi.s_img = 0;
+  p.epi.s_pix = ldc;
+  p.epi.s_ch = 1;
+
+  CUtensorMap tA, tW, tH[4];
+  std::memset(tH, 0, sizeof(tH));
+  {
+    const uint64_t dims[2] = {uint64_t(K), uint64_t(M)};
+    const uint64_t str[1] = {uint64_t(lda)};
+    const uint32_t box[2] = {uint32_t(kBK), uint32_t(kBM)};
+    if (encode_u8(&tA, A, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return W4A8_ERR_TENSORMAP;
+  }
+  {
+    const uint64_t dims[2] = {uint64_t(i4 ? K / 2 : K), uint64_t(N)};
+    const uint64_t str[1] = {uint64_t(ldw)};
+    const uint32_t box[2] = {uint32_t(i4 ? kBK / 2 : kBK), uint32_t(bn)};
+    if (encode_u8(&tW, W, 2, dims, str, box, i4 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B))
+      return W4A8_ERR_TENSORMAP;
+  }
+  const int grid = std::min(p.tiles_m * p.tiles_n, sms);
+  return launch(i4, false, bn, tA, tW, tH, p, grid, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t ldw, const w4a8_conv_geom* g,
+                           const w4a8_epilogue* epi, void* out, void* stream) {
+  if (!g) return W4A8_ERR_ARG;
+  if (w_kind != W4A8_W_INT8 && w_kind != W4A8_W_INT4) return W4A8_ERR_ARG;
+  const bool i4 = w_kind == W4A8_W_INT4;
+  if (int rc = check_epilogue(epi)) return rc;
+  if (g->n < 0 || g->h < 1 || g->w < 1 || g->c < 16 || g->kh < 1 || g->kw < 1 || g->ho < 1 || g->wo < 1 ||
+      g->o < 1 || g->pad_h < 0 || g->pad_w < 0)
+    return W4A8_ERR_ARG;
+  if (g->stride != 1 && g->stride != 2) return W4A8_ERR_UNSUPPORTED;
+  if (g->c % 16) return W4A8_ERR_ALIGN;
+  // A 32-byte MMA K-step must read one tap (or, for c == 16, a tap pair).
+  if (g->c != 16 && (g->c % 32 || (g->c > 128 && g->c % 128))) return W4A8_ERR_UNSUPPORTED;
+  if (g->out_layout != W4A8_LAYOUT_NHWC && g->out_layout != W4A8_LAYOUT_NCHW) return W4A8_ERR_ARG;
+  if (g->out_layout == W4A8_LAYOUT_NHWC && g->ldo < g->o) return W4A8_ERR_ARG;
+  if (g->n == 0) return W4A8_OK;
+  if (!x || !W || !out) return W4A8_ERR_ARG;
+  const int s = g->stride;
+  const int taps = g->kh * g->kw;
+  const long long k_total = (long long)taps * g->c;
+  if (ldw < (i4 ? k_total / 2 : k_total)) return W4A8_ERR_ARG;
+  if ((ldw % 16) || !aligned16(x) || !aligned16(W)) return W4A8_ERR_ALIGN;
+  // Every output pixel must read at least one in-bounds row/column window.
+  if ((long long)(g->ho - 1) * s - g->pad_h >= g->h || (long long)(g->wo - 1) * s - g->pad_w >= g->w)
+    return W4A8_ERR_ARG;
+
+  const int cg = g->c < 128 ? g->c : 128;
+  const int groups = g->c / cg;
+  const int planes = cg / 16;
+  const int kbpg = (taps * cg + kBK - 1) / kBK;
+  const int steps = kbpg * (kBK / 32);
+  if (steps > kMaxSteps) return W4A8_ERR_UNSUPPORTED;
+
+  // Stride phases (sub-tiles) and their offsets in phase-view units.
+  int qmin_h[2] = {1 << 20, 1 << 20}, qmax_h[2] = {-(1 << 20), -(1 << 20)};
+  int qmin_w[2] = {1 << 20, 1 << 20}, qmax_w[2] = {-(1 << 20), -(1 << 20)};
+  bool used[2][2] = {{false, false}, {false, false}};
+  for (int ky = 0; ky < g->kh; ++ky)
+    for (int kx = 0; kx < g->kw; ++kx) {
+      const int dy = ky - g->pad_h, dx = kx - g->pad_w;
+      const int qy = floordiv(dy, s), py = dy - qy * s;
+      const int qx = floordiv(dx, s), px = dx - qx * s;
+      used[py][px] = true;
+      qmin_h[py] = std::min(qmin_h[py], qy);
+      qmax_h[py] = std::max(qmax_h[py], qy);
+      qmin_w[px] = std::min(qmin_w[px], qx);
+      qmax_w[px] = std::max(qmax_w[px], qx);
+    }
+  int span_h = 0, span_w = 0;
+  for (int i = 0; i < s; ++i) {
+    if (qmax_h[i] >= qmin_h[i]) span_h = std::max(span_h, qmax_h[i] - qmin_h[i]);
+    if (qmax_w[i] >= qmin_w[i]) span_w = std::max(span_w, qmax_w[i] - qmin_w[i]);
+  }
+  KParams p;
+  std::memset(&p, 0, sizeof(p));
+  ConvParams& cp = p.conv;
+  cp.ho = g->ho;
+  cp.wo = g->wo;
+  cp.tiles_h = (g->ho + kTileH - 1) / kTileH;
+  cp.tiles_w = (g->wo + kTileW - 1) / kTileW;
+  cp.planes = planes;
+  cp.halo_w = kTileW + span_w;
+  cp.halo_h = kTileH + span_h;
+  if (cp.halo_w > 256 || cp.halo_h > 256) return W4A8_ERR_UNSUPPORTED;
+  cp.plane_bytes = (uint32_t(cp.halo_w * cp.halo_h * 16) + 127u) & ~127u;
+  cp.slot_bytes = cp.plane_bytes * planes;
+  int slot_of[2][2] = {{-1, -1}, {-1, -1}};
+  int slot_py[4], slot_px[4];
+  int ns = 0;
+  for (int py = 0; py < s; ++py)
+    for (int px = 0; px < s; ++px)
+      if (used[py][px]) {
+        slot_of[py][px] = ns;
+        slot_py[ns] = py;
+        slot_px[ns] = px;
+        cp.slot_qh[ns] = qmin_h[py];
+        cp.slot_qw[ns] = qmin_w[px];
+        ++ns;
+      }
+  cp.n_slots = ns;
+  cp.halo_bytes = (cp.slot_bytes * ns + 1023u) & ~1023u;
+  cp.halo_tx_bytes = uint32_t(ns * planes * cp.halo_w * cp.halo_h * 16);
+  cp.kb_per_group = kbpg;
+  auto chunk_off = [&](int k) -> long long {
+    const int t = k / cg, c = (k % cg) / 16;
+    const int ky = t / g->kw, kx = t % g->kw;
+    const int dy = ky - g->pad_h, dx = kx - g->pad_w;
+    const int qy = floordiv(dy, s), py = dy - qy * s;
+    const int qx = floordiv(dx, s), px = dx - qx * s;
+    const int sl = slot_of[py][px];
+    const int pix = (qy - qmin_h[py]) * cp.halo_w + (qx - qmin_w[px]);
+    return (long long)sl * cp.slot_bytes + (long long)c * cp.plane_bytes + (long long)pix * 16;
+  };
+  for (int j = 0; j < steps; ++j) {
+    const int k = 32 * j;
+    if (k >= taps * cg) {
+      cp.step_off[j] = cp.step_off[0];
+      cp.step_lbo[j] = cp.step_lbo[0];
+      continue;
+    }
+    const long long o1 = chunk_off(k);
+    long long lbo = 16;
+    if (k + 16 < taps * cg) lbo = chunk_off(k + 16) - o1;
+    if (lbo <= 0 || (lbo % 16) || lbo >= (1 << 18)) return W4A8_ERR_UNSUPPORTED;
+    cp.step_off[j] = uint32_t(o1);
+    cp.step_lbo[j] = uint32_t(lbo);
+  }
+
+  const int sms = device_sms();
+  const int bn = g->o <= 64 ? 64 : (g->o <= 128 ? 128 : 256);
+  p.M = 0;
+  p.N = g->o;
+  p.num_kb = groups * kbpg;
+  p.tiles_m = g->n * cp.tiles_h * cp.tiles_w;
+  p.tiles_n = (g->o + bn - 1) / bn;
+  p.a_stage_bytes = 0;
+  p.b_stage_bytes = bn * kBK;
+  p.bp_stage_bytes = i4 ? bn * kBK / 2 : 0;
+  const uint32_t per_stage = p.b_stage_bytes + p.bp_stage_bytes;
+  p.halo_stages = 2;
+  p.stages = pick_stages(per_stage, 2 * cp.halo_bytes);
+  if (p.stages < 3) {
+    p.halo_stages = 1;
+    p.stages = pick_stages(per_stage, cp.halo_bytes);
+  }
+  if (p.stages < 2) return W4A8_ERR_UNSUPPORTED;
+  p.a_off = 0;
+  p.h_off = 0;
+  p.b_off = p.halo_stages * cp.halo_bytes;
+  p.bp_off = p.b_off + p.stages * p.b_stage_bytes;
+  p.tx_bytes = i4 ? p.bp_stage_bytes : p.b_stage_bytes;
+  p.tmem_cols = 2 * bn;
+  p.err = device_error_word();
+  if (!p.err) return W4A8_ERR_LAUNCH;
+  fill_epi(p.epi, epi, out, g->o);
+  if (g->out_layout == W4A8_LAYOUT_NHWC) {
+    p.epi.s_img = (long long)g->ho * g->wo * g->ldo;
+    p.epi.s_pix = g->ldo;
+    p.epi.s_ch = 1;
+  } else {
+    p.epi.s_img = (long long)g->o * g->ho * g->wo;
+    p.epi.s_pix = 1;
+    p.epi.s_ch = (long long)g->ho * g->wo;
+  }
+
+  CUtensorMap tA, tW, tH[4];
+  std::memset(&tA, 0, sizeof(tA));
+  std::memset(tH, 0, sizeof(tH));
+  {
+    const uint64_t dims[2] = {uint64_t(i4 ? k_total / 2 : k_total), uint64_t(g->o)};
+    const uint64_t str[1] = {uint64_t(ldw)};
+    const uint32_t box[2] = {uint32_t(i4 ? kBK / 2 : kBK), uint32_t(bn)};
+    if (encode_u8(&tW, W, 2, dims, str, box, i4 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B))
+      return W4A8_ERR_TENSORMAP;
+  }
+  for (int sl = 0; sl < ns; ++sl) {
+    const int py = slot_py[sl], px = slot_px[sl];
+    const int8_t* base = x + ((long long)py * g->w + px) * g->c;
+    const uint64_t dims[5] = {16, uint64_t(g->c / 16), uint64_t((g->w - px + s - 1) / s),
+                              uint64_t((g->h - py + s - 1) / s), uint64_t(g->n)};
+    const uint64_t str[4] = {16, uint64_t(s) * g->c, uint64_t(s) * g->w * g->c, uint64_t(g->h) * g->w * g->c};
+    const uint32_t box[5] = {16, 1, uint32_t(cp.halo_w), uint32_t(cp.halo_h), 1};
+    if (encode_u8(&tH[sl], base, 5, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)) return W4A8_ERR_TENSORMAP;
+  }
+  const int grid = std::min(p.tiles_m * p.tiles_n, sms);
+  return launch(i4, true, bn, tA, tW, tH, p, grid, static_cast<cudaStream_t>(stream));
+}

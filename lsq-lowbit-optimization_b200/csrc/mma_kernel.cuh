@@ -1,0 +1,432 @@
+// Persistent, warp-specialised tcgen05 int8 kernel shared by the W4A8 GEMM
+// and the implicit-GEMM NHWC convolution.
+//
+//   D[128 x BN] (int32, TMEM) = A[128 x K] (int8, smem) . B[BN x K]^T (int8, smem)
+//
+// Rows of A are GEMM rows (GEMM mode) or a 16x8 block of output pixels of
+// one image (conv mode); columns are output features / channels.
+//
+// Warp roles (384 threads):
+//   warp 0      TMA producer (one elected lane)
+//   warp 1      TMEM owner + MMA issuer (one elected lane)
+//   warps 4-7   epilogue: tcgen05.ld -> fused LSQ epilogue -> global stores
+//   warps 8-11  int4 unpack: packed nibbles (smem, TMA) -> int8 SW128 tile
+// The accumulator is double-buffered in TMEM so the epilogue of tile i
+// overlaps the main loop of tile i+1.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "ptx.cuh"
+
+namespace w4a8 {
+
+constexpr int kBM = 128;          // rows per tile (MMA M)
+constexpr int kBK = 128;          // K bytes per k-block (one 128B swizzle atom)
+constexpr int kThreads = 384;
+constexpr int kMaxStages = 8;
+constexpr int kMaxHaloStages = 2;
+constexpr int kMaxSteps = 64;     // conv MMA K-steps (32 B) per channel group
+constexpr int kTileH = 16;        // conv: output rows per tile (one 8-row core group each)
+constexpr int kTileW = 8;         // conv: output columns per tile
+
+struct EpiParams {
+  void* out;
+  int out_kind;  // 0 s32, 1 f32, 2 f16, 3 s8
+  int relu;
+  const float* alpha;
+  float alpha_scalar;
+  const float* beta;
+  const float* residual;
+  long long res_ld;
+  float out_scale;
+  int qn, qp;
+  float* aux;
+  long long aux_ld;
+  long long s_img, s_pix, s_ch;  // output element strides
+  int n_total;                   // valid columns
+};
+
+struct ConvParams {
+  int ho, wo;              // output size
+  int tiles_h, tiles_w;    // tiles per image
+  int n_slots;             // halo sub-tiles (stride phases) in use
+  int planes;              // 16-byte channel planes per group
+  int halo_w, halo_h;      // sub-halo size in pixels
+  uint32_t plane_bytes;    // bytes per plane (128-aligned)
+  uint32_t slot_bytes;     // planes * plane_bytes
+  uint32_t halo_bytes;     // 1024-aligned bytes per halo stage
+  uint32_t halo_tx_bytes;  // bytes the TMA loads of one stage deliver
+  int slot_qh[4], slot_qw[4];  // per slot: TMA start offset in phase-view units
+  int kb_per_group;
+  uint32_t step_off[kMaxSteps];  // smem byte offset of the first 16 B K-chunk
+  uint32_t step_lbo[kMaxSteps];  // byte distance to the second 16 B K-chunk
+};
+
+struct KParams {
+  int M, N;
+  int num_kb;        // k-blocks per tile
+  int tiles_m, tiles_n;
+  int stages;        // operand pipeline depth
+  int halo_stages;   // conv halo pipeline depth
+  uint32_t a_off, b_off, bp_off, h_off;  // smem region offsets (from 1024-aligned base)
+  uint32_t a_stage_bytes, b_stage_bytes, bp_stage_bytes;
+  uint32_t tx_bytes;  // TMA bytes per operand stage
+  uint32_t tmem_cols;
+  unsigned* err;
+  EpiParams epi;
+  ConvParams conv;
+};
+
+// ----------------------------- epilogue ------------------------------------
+__device__ __forceinline__ void store16_f32(float* dst, const float (&v)[16], int ncols, long long s_ch) {
+  if (ncols == 16 && s_ch == 1 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  } else {
+    for (int i = 0; i < ncols; ++i) dst[i * s_ch] = v[i];
+  }
+}
+
+__device__ __forceinline__ void epilogue_chunk(const EpiParams& e, const uint32_t (&acc)[16], int n, long long out_off,
+                                               long long prow) {
+  const int ncols = min(16, e.n_total - n);
+  if (ncols <= 0) return;
+  if (e.out_kind == 0) {
+    int32_t* dst = static_cast<int32_t*>(e.out) + out_off;
+    if (ncols == 16 && e.s_ch == 1 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+      int4* d4 = reinterpret_cast<int4*>(dst);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        d4[i] = make_int4(int(acc[4 * i]), int(acc[4 * i + 1]), int(acc[4 * i + 2]), int(acc[4 * i + 3]));
+    } else {
+      for (int i = 0; i < ncols; ++i) dst[i * e.s_ch] = int(acc[i]);
+    }
+    return;
+  }
+  float y[16];
+  const float* res = e.residual ? e.residual + prow * e.res_ld + n : nullptr;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    if (i < ncols) {
+      const float a = e.alpha ? __ldg(e.alpha + n + i) : e.alpha_scalar;
+      float v = __fmul_rn(__int2float_rn(int(acc[i])), a);
+      if (e.beta) v = __fadd_rn(v, __ldg(e.beta + n + i));
+      if (res) v = __fadd_rn(v, res[i]);
+      if (e.relu) v = fmaxf(v, 0.0f);
+      y[i] = v;
+    } else {
+      y[i] = 0.0f;
+    }
+  }
+  if (e.aux) store16_f32(e.aux + prow * e.aux_ld + n, y, ncols, 1);
+  if (e.out_kind == 1) {
+    store16_f32(static_cast<float*>(e.out) + out_off, y, ncols, e.s_ch);
+  } else if (e.out_kind == 2) {
+    __half* dst = static_cast<__half*>(e.out) + out_off;
+    if (ncols == 16 && e.s_ch == 1 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+      uint32_t w[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const __half lo = __float2half_rn(y[2 * i]);
+        const __half hi = __float2half_rn(y[2 * i + 1]);
+        w[i] = uint32_t(__half_as_ushort(lo)) | (uint32_t(__half_as_ushort(hi)) << 16);
+      }
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+      d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    } else {
+      for (int i = 0; i < ncols; ++i) dst[i * e.s_ch] = __float2half_rn(y[i]);
+    }
+  } else {
+    int8_t* dst = static_cast<int8_t*>(e.out) + out_off;
+    uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      int q = __float2int_rn(__fdiv_rn(y[i], e.out_scale));
+      q = max(e.qn, min(e.qp, q));
+      w[i >> 2] |= (uint32_t(q) & 0xFFu) << (8 * (i & 3));
+    }
+    if (ncols == 16 && e.s_ch == 1 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      for (int i = 0; i < ncols; ++i) dst[i * e.s_ch] = int8_t((w[i >> 2] >> (8 * (i & 3))) & 0xFFu);
+    }
+  }
+}
+
+// Maps (tile m index, row within tile) to output addressing.
+template <bool kConv>
+__device__ __forceinline__ bool row_coords(const KParams& p, int mt, int m, long long& out_off,
+                                           long long& prow) {
+  if constexpr (!kConv) {
+    const int row = mt * kBM + m;
+    out_off = (long long)row * p.epi.s_pix;
+    prow = row;
+    return row < p.M;
+  } else {
+    const ConvParams& c = p.conv;
+    const int per_img = c.tiles_h * c.tiles_w;
+    const int img = mt / per_img;
+    const int rem = mt - img * per_img;
+    const int th = rem / c.tiles_w;
+    const int tw = rem - th * c.tiles_w;
+    const int oh = th * kTileH + (m >> 3);
+    const int ow = tw * kTileW + (m & 7);
+    const long long pix = (long long)oh * c.wo + ow;
+    out_off = (long long)img * p.epi.s_img + pix * p.epi.s_pix;
+    prow = (long long)img * c.ho * c.wo + pix;
+    return oh < c.ho && ow < c.wo;
+  }
+}
+
+// ------------------------------ kernel -------------------------------------
+template <int BN, bool kInt4, bool kConv>
+__global__ void __launch_bounds__(kThreads, 1)
+    w4a8_mma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                    const __grid_constant__ CUtensorMap tmH0, const __grid_constant__ CUtensorMap tmH1,
+                    const __grid_constant__ CUtensorMap tmH2, const __grid_constant__ CUtensorMap tmH3,
+                    const __grid_constant__ KParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bar_full[kMaxStages];
+  __shared__ __align__(8) uint64_t bar_ready[kMaxStages];
+  __shared__ __align__(8) uint64_t bar_empty[kMaxStages];
+  __shared__ __align__(8) uint64_t bar_hfull[kMaxHaloStages];
+  __shared__ __align__(8) uint64_t bar_hempty[kMaxHaloStages];
+  __shared__ __align__(8) uint64_t bar_tfull[2];
+  __shared__ __align__(8) uint64_t bar_tempty[2];
+  __shared__ __align__(8) uint64_t bar_drain;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t base_u32 = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* base = smem_raw + (base_u32 - smem_u32(smem_raw));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&bar_full[s], 1);
+      mbar_init(&bar_ready[s], 128);
+      mbar_init(&bar_empty[s], 1);
+    }
+    for (int s = 0; s < p.halo_stages; ++s) {
+      mbar_init(&bar_hfull[s], 1);
+      mbar_init(&bar_hempty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar_tfull[b], 1);
+      mbar_init(&bar_tempty[b], 128);
+    }
+    mbar_init(&bar_drain, 1);
+    abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmW);
+    if constexpr (!kConv) tma_prefetch_desc(&tmA);
+  }
+  if (kConv && threadIdx.x >= 32 && threadIdx.x < 64) {
+    // Zero the halo buffers once: rows a sub-tile box does not cover stay 0.
+    for (uint32_t i = (threadIdx.x - 32) * 16; i < p.conv.halo_bytes * p.halo_stages; i += 32 * 16)
+      *reinterpret_cast<uint4*>(base + p.h_off + i) = make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_slot, p.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+
+  const int total_tiles = p.tiles_m * p.tiles_n;
+  const int kbpg = kConv ? p.conv.kb_per_group : p.num_kb;
+
+  if (warp == 0) {
+    // ---------------------------- producer ----------------------------------
+    if (lane == 0) {
+      int s = 0, hs = 0;
+      uint32_t ph = 0, hph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+        const int mt = t / p.tiles_n;
+        const int nt = t - mt * p.tiles_n;
+        int img = 0, oh0 = 0, ow0 = 0;
+        if constexpr (kConv) {
+          const int per_img = p.conv.tiles_h * p.conv.tiles_w;
+          img = mt / per_img;
+          const int rem = mt - img * per_img;
+          const int th = rem / p.conv.tiles_w;
+          oh0 = th * kTileH;
+          ow0 = (rem - th * p.conv.tiles_w) * kTileW;
+        }
+        for (int kb = 0; ok && kb < p.num_kb; ++kb) {
+          if constexpr (kConv) {
+            if (kb % kbpg == 0) {
+              const int g = kb / kbpg;
+              if (!mbar_wait(&bar_hempty[hs], hph ^ 1, &abort_flag)) { ok = false; break; }
+              mbar_arrive_expect_tx(&bar_hfull[hs], p.conv.halo_tx_bytes);
+              uint8_t* hdst = base + p.h_off + hs * p.conv.halo_bytes;
+              for (int sl = 0; sl < p.conv.n_slots; ++sl) {
+                const CUtensorMap* m = sl == 0 ? &tmH0 : sl == 1 ? &tmH1 : sl == 2 ? &tmH2 : &tmH3;
+                for (int pl = 0; pl < p.conv.planes; ++pl)
+                  tma_load_5d(hdst + sl * p.conv.slot_bytes + pl * p.conv.plane_bytes, m, &bar_hfull[hs], 0,
+                              g * p.conv.planes + pl, ow0 + p.conv.slot_qw[sl], oh0 + p.conv.slot_qh[sl], img);
+              }
+              if (++hs == p.halo_stages) { hs = 0; hph ^= 1; }
+            }
+          }
+          if (!mbar_wait(&bar_empty[s], ph ^ 1, &abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bar_full[s], p.tx_bytes);
+          if constexpr (!kConv) tma_load_2d(base + p.a_off + s * p.a_stage_bytes, &tmA, &bar_full[s], kb * kBK, mt * kBM);
+          if constexpr (kInt4)
+            tma_load_2d(base + p.bp_off + s * p.bp_stage_bytes, &tmW, &bar_full[s], kb * (kBK / 2), nt * BN);
+          else
+            tma_load_2d(base + p.b_off + s * p.b_stage_bytes, &tmW, &bar_full[s], kb * kBK, nt * BN);
+          if (++s == p.stages) { s = 0; ph ^= 1; }
+        }
+      }
+      // Drain: every TMA this thread issued has landed before the CTA exits.
+      for (int i = 0; i < p.stages; ++i) {
+        const int idx = (s + p.stages - 1 - i) % p.stages;
+        const uint32_t par = (idx < s) ? ph : (ph ^ 1);
+        const unsigned long long t0 = global_timer_ns();
+        while (!mbar_try_wait(&bar_full[idx], par))
+          if (global_timer_ns() - t0 > kWaitLimitNs) { abort_flag = 1; break; }
+      }
+      for (int i = 0; kConv && i < p.halo_stages; ++i) {
+        const int idx = (hs + p.halo_stages - 1 - i) % p.halo_stages;
+        const uint32_t par = (idx < hs) ? hph : (hph ^ 1);
+        const unsigned long long t0 = global_timer_ns();
+        while (!mbar_try_wait(&bar_hfull[idx], par))
+          if (global_timer_ns() - t0 > kWaitLimitNs) { abort_flag = 1; break; }
+      }
+      if (!ok) atomicOr(p.err, kErrTimeoutProducer);
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA ------------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_i8(kBM, BN);
+      int s = 0, hs = 0, it = 0;
+      uint32_t ph = 0, hph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x, ++it) {
+        const int buf = it & 1;
+        if (!mbar_wait(&bar_tempty[buf], ((it >> 1) & 1) ^ 1, &abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        uint32_t halo_addr = 0;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if constexpr (kConv) {
+            if (kb % kbpg == 0) {
+              if (!mbar_wait(&bar_hfull[hs], hph, &abort_flag)) { ok = false; break; }
+              halo_addr = base_u32 + p.h_off + hs * p.conv.halo_bytes;
+            }
+          }
+          if (!mbar_wait(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t b_addr = base_u32 + p.b_off + s * p.b_stage_bytes;
+#pragma unroll
+          for (int j = 0; j < kBK / 32; ++j) {
+            uint64_t a_desc;
+            if constexpr (kConv) {
+              const int step = (kb % kbpg) * 4 + j;
+              a_desc = make_smem_desc(halo_addr + p.conv.step_off[step], p.conv.step_lbo[step],
+                                      p.conv.halo_w * 16, kLayoutNone);
+            } else {
+              a_desc = make_smem_desc(base_u32 + p.a_off + s * p.a_stage_bytes + j * 32, 16, 1024, kLayoutSw128);
+            }
+            const uint64_t b_desc = make_smem_desc(b_addr + j * 32, 16, 1024, kLayoutSw128);
+            mma_i8_ss(d_tmem, a_desc, b_desc, idesc, (kb | j) != 0 ? 1u : 0u);
+          }
+          mma_commit(&bar_empty[s]);
+          if constexpr (kConv) {
+            if (kb % kbpg == kbpg - 1) {
+              mma_commit(&bar_hempty[hs]);
+              if (++hs == p.halo_stages) { hs = 0; hph ^= 1; }
+            }
+          }
+          if (++s == p.stages) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit(&bar_tfull[buf]);
+      }
+      // Drain: all tcgen05 ops of this thread complete before TMEM is freed.
+      mma_commit(&bar_drain);
+      const unsigned long long t0 = global_timer_ns();
+      while (!mbar_try_wait(&bar_drain, 0))
+        if (global_timer_ns() - t0 > kWaitLimitNs) { atomicOr(p.err, kErrTimeoutDrain); break; }
+      if (!ok) atomicOr(p.err, kErrTimeoutMma);
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ----------------------------- epilogue --------------------------------
+    const int q = warp - 4;
+    const int m = q * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
+      const int buf = it & 1;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&bar_tfull[buf], (it >> 1) & 1, &abort_flag) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) atomicOr(p.err, kErrTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after();
+      const int mt = t / p.tiles_n;
+      const int nt = t - mt * p.tiles_n;
+      long long out_off = 0, prow = 0;
+      const bool valid = row_coords<kConv>(p, mt, m, out_off, prow);
+      const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t acc[16];
+        tmem_ld16(t_addr + c0, acc);
+        tmem_ld_wait();
+        const int n = nt * BN + c0;
+        if (valid) epilogue_chunk(p.epi, acc, n, out_off + (long long)n * p.epi.s_ch, prow);
+      }
+      tc_fence_before();
+      mbar_arrive(&bar_tempty[buf]);
+    }
+  } else if (warp >= 8 && kInt4) {
+    // ------------------------------ unpack ---------------------------------
+    const int ut = threadIdx.x - 256;
+    int s = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        if (!mbar_wait(&bar_full[s], ph, &abort_flag)) { ok = false; break; }
+        const uint8_t* src = base + p.bp_off + s * p.bp_stage_bytes;
+        uint8_t* dst = base + p.b_off + s * p.b_stage_bytes;
+#pragma unroll 4
+        for (int idx = ut; idx < BN * 8; idx += 128) {
+          const int r = idx >> 3;
+          const int c = idx & 7;
+          const uint2 v = *reinterpret_cast<const uint2*>(src + r * 64 + c * 8);
+          uint4 o;
+          unpack_nibbles8(v.x, o.x, o.y);
+          unpack_nibbles8(v.y, o.z, o.w);
+          *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = o;
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&bar_ready[s]);
+        if (++s == p.stages) { s = 0; ph ^= 1; }
+      }
+    }
+    if (!ok && ut == 0) atomicOr(p.err, kErrTimeoutUnpack);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, p.tmem_cols);
+  }
+}
+
+}  // namespace w4a8

@@ -1,0 +1,158 @@
+"""Implicit-GEMM NHWC convolution and the reference's conv ops vs the oracle."""
+import numpy as np
+import pytest
+import torch
+
+import int4_int8_ext as ext
+from oracle import oracle as orc
+from tests.helpers import assert_close, assert_equal, rand_i4, rand_i8, rng, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+def kernel_order_weights(w_ohwi: np.ndarray) -> np.ndarray:
+    """OHWI weights -> the conv kernel's [o, groups, taps, 128] order (identity for c <= 128)."""
+    o, kh, kw, c = w_ohwi.shape
+    if c <= 128:
+        return w_ohwi.reshape(o, -1)
+    g = c // 128
+    return w_ohwi.reshape(o, kh * kw, g, 128).transpose(0, 2, 1, 3).reshape(o, -1)
+
+
+def run_nhwc_conv(cuda, xq, w_ohwi, stride, pad, ho, wo, epi_kw, out_kind, int4=True):
+    n, h, w, c = xq.shape
+    o, kh, kw, _ = w_ohwi.shape
+    wk = kernel_order_weights(w_ohwi)
+    if int4:
+        wdev = orc.pack_int4(wk)
+        ld = -(-wdev.shape[1] // 16) * 16
+        wpad = np.zeros((o, ld), np.uint8)
+        wpad[:, : wdev.shape[1]] = wdev
+        kind = ext.W_INT4
+    else:
+        ld = -(-wk.shape[1] // 16) * 16
+        wpad = np.zeros((o, ld), np.int8)
+        wpad[:, : wk.shape[1]] = wk
+        kind = ext.W_INT8
+    dtype = {ext.OUT_S32: torch.int32, ext.OUT_F32: torch.float32, ext.OUT_S8: torch.int8,
+             ext.OUT_F16: torch.float16}[out_kind]
+    out = torch.empty((n, ho, wo, o), dtype=dtype, device=cuda)
+    geom = ext.ConvGeom(n, h, w, c, kh, kw, stride, pad, pad, ho, wo, o, ext.LAYOUT_NHWC, o)
+    epi = ext.make_epilogue(out_kind, **epi_kw)
+    ext.conv2d_nhwc(to_dev(xq, cuda), to_dev(wpad, cuda), kind, geom, epi, out)
+    return out
+
+
+CONV_CASES = [
+    # n, h, w, c, o, k, stride, pad
+    (2, 10, 10, 16, 64, 3, 1, 1),
+    (2, 14, 14, 64, 64, 3, 1, 1),
+    (1, 56, 56, 64, 64, 3, 1, 1),
+    (2, 28, 28, 128, 128, 3, 1, 1),
+    (2, 14, 14, 256, 256, 3, 1, 1),
+    (2, 7, 7, 512, 512, 3, 1, 1),
+    (2, 56, 56, 64, 128, 3, 2, 1),
+    (2, 28, 28, 128, 256, 3, 2, 1),
+    (2, 14, 14, 256, 512, 3, 2, 1),
+    (2, 56, 56, 64, 128, 1, 2, 0),
+    (2, 14, 14, 256, 512, 1, 2, 0),
+    (2, 9, 13, 32, 48, 1, 1, 0),
+    (2, 11, 9, 96, 80, 3, 1, 1),
+    (2, 12, 10, 16, 32, 3, 2, 1),
+]
+
+
+@pytest.mark.parametrize("n,h,w,c,o,k,stride,pad", CONV_CASES)
+def test_conv_nhwc_s32_bitexact(cuda, n, h, w, c, o, k, stride, pad):
+    g = rng(n * 1000 + h * 10 + c + o + k + stride)
+    xq = rand_i8(g, (n, h, w, c), 0, 127)
+    wt = rand_i4(g, (o, k, k, c))
+    ho = (h + 2 * pad - k) // stride + 1
+    wo = (w + 2 * pad - k) // stride + 1
+    got = run_nhwc_conv(cuda, xq, wt, stride, pad, ho, wo, {}, ext.OUT_S32)
+    want = orc.conv_nhwc_s32(xq, wt, stride, pad, pad, ho, wo)
+    assert_equal(got, want, f"conv {n},{h},{w},{c}->{o} k{k}s{stride}")
+    assert ext.device_error() == 0
+
+
+def test_conv_channel_rule(cuda):
+    """c = 48 splits a 32-byte K-step across taps: rejected, not miscomputed."""
+    g = rng(9)
+    xq = rand_i8(g, (1, 8, 8, 48), 0, 127)
+    wt = rand_i4(g, (16, 3, 3, 48))
+    with pytest.raises(RuntimeError, match="status 3"):
+        run_nhwc_conv(cuda, xq, wt, 1, 1, 8, 8, {}, ext.OUT_S32)
+
+
+def test_stem_s2d_conv(cuda):
+    """4x4 conv, pad 2 top/left, 16 channels: the space-to-depth stem."""
+    g = rng(77)
+    xq = rand_i8(g, (2, 32, 32, 16))
+    wt = rand_i8(g, (64, 4, 4, 16))
+    got = run_nhwc_conv(cuda, xq, wt, 1, 2, 32, 32, {}, ext.OUT_S32, int4=False)
+    assert_equal(got, orc.conv_nhwc_s32(xq, wt, 1, 2, 2, 32, 32), "stem s2d")
+
+
+def test_conv_fused_requant_epilogue(cuda):
+    """Config-2 style layer (reduced batch): 3x3 s1 p1 64->64, per-channel
+    scale, bias, ReLU, requant to int8 with scale 0.05."""
+    g = rng(2)
+    n, h, w, c, o = 4, 56, 56, 64, 64
+    xq = rand_i8(g, (n, h, w, c), 0, 127)
+    wt = rand_i4(g, (o, 3, 3, c))
+    s_w = g.uniform(1e-3, 1e-2, o).astype(np.float32)
+    bias = g.normal(0, 0.01, o).astype(np.float32)
+    alpha = (np.float64(0.05) * s_w.astype(np.float64)).astype(np.float32)
+    acc = orc.conv_nhwc_s32(xq, wt, 1, 1, 1, h, w)
+    want = orc.quantize(orc.epilogue(acc, alpha, bias, relu=True), 0.05, 0, 127)
+    epi = dict(alpha=to_dev(alpha, cuda), beta=to_dev(bias, cuda), relu=True, out_scale=0.05, qn=0, qp=127)
+    got = run_nhwc_conv(cuda, xq, wt, 1, 1, h, w, epi, ext.OUT_S8)
+    assert_equal(got, want, "requant conv")
+
+
+def test_conv3x3_op_matches_oracle(cuda):
+    g = rng(3)
+    for (n, c, h, w, o) in [(2, 3, 10, 12, 16), (2, 16, 9, 9, 32), (1, 64, 20, 17, 64), (2, 130, 8, 8, 24)]:
+        x = g.normal(0, 2, (n, c, h, w)).astype(np.float32)
+        k = c * 9 + (c * 9) % 2
+        wt = rand_i4(g, (o, k))
+        wt[:, c * 9:] = 0
+        bp = orc.pack_int4(wt)
+        bias = g.normal(0, 0.1, o).astype(np.float32)
+        for half in (False, True):
+            got = ext.conv3x3_int4_int8_s1_p1(to_dev(x, cuda), to_dev(bp, cuda), 0.05, 0.02, -127, 127,
+                                              to_dev(bias, cuda), half)
+            want = orc.conv3x3_s1_p1(x, bp, 0.05, 0.02, -127, 127, bias, half)
+            assert_equal(got, want, f"conv3x3 op c={c} half={half}")
+
+
+def test_conv3x3_op_zero_outside_range(cuda):
+    """qn > 0: the reference's lowering pads with the code of 0.0 (= qn)."""
+    g = rng(4)
+    x = g.normal(0, 2, (2, 16, 8, 8)).astype(np.float32)
+    wt = rand_i4(g, (32, 144))
+    bp = orc.pack_int4(wt)
+    got = ext.conv3x3_int4_int8_s1_p1(to_dev(x, cuda), to_dev(bp, cuda), 0.05, 0.02, 3, 100, None, False)
+    assert_equal(got, orc.conv3x3_s1_p1(x, bp, 0.05, 0.02, 3, 100, None, False), "qn>0 padding")
+
+
+def test_conv1x1_op_matches_oracle(cuda):
+    g = rng(6)
+    for (n, c, h, w, o, sh, sw) in [(2, 64, 14, 14, 128, 2, 2), (2, 32, 9, 11, 16, 1, 1), (1, 16, 10, 10, 32, 3, 2)]:
+        x = g.normal(0, 2, (n, c, h, w)).astype(np.float32)
+        bp = orc.pack_int4(rand_i4(g, (o, c)))
+        bias = g.normal(0, 0.1, o).astype(np.float32)
+        got = ext.conv1x1_int4_int8(to_dev(x, cuda), to_dev(bp, cuda), 0.05, 0.02, -128, 127, sh, sw,
+                                    to_dev(bias, cuda), False)
+        want = orc.conv1x1(x, bp, 0.05, 0.02, -128, 127, sh, sw, bias, False)
+        assert_equal(got, want, f"conv1x1 s{sh}{sw}")
+        assert_close(got, want, 1e-3)
+
+
+def test_lower_quantize_3x3_matches_oracle(cuda):
+    g = rng(8)
+    x = g.normal(0, 2, (2, 5, 7, 6)).astype(np.float32)
+    got = ext.lower_quantize_3x3_s1_p1(to_dev(x, cuda), 0.05, -128, 127, 50)
+    assert_equal(got, orc.lower_quantize_3x3(x, 0.05, -128, 127, 50), "lowering")
+    got = ext.lower_quantize_3x3_s1_p1(to_dev(x, cuda), 0.05, 2, 127, 46)
+    assert_equal(got, orc.lower_quantize_3x3(x, 0.05, 2, 127, 46), "lowering qn>0")
