@@ -219,10 +219,11 @@ def repack_oihw_int4(w_packed: torch.Tensor, c: int, kh: int, kw: int, c_pad: in
     return out
 
 
-def conv_channels_padded(c: int) -> int:
-    """Channel count the conv kernel accepts: 16, a multiple of 32 up to 128,
-    or a multiple of 128 (a 32-byte MMA K-step must stay on one tap)."""
-    if c <= 16:
+def conv_channels_padded(c: int, stride: int = 1) -> int:
+    """Channel count the conv kernel accepts: 16 (stride 1 only), a multiple
+    of 32 up to 128, or a multiple of 128. A 32-byte MMA K-step must read
+    one tap, or for 16 channels two taps of one stride phase."""
+    if c <= 16 and stride == 1:
         return 16
     return _round_up(c, 32) if c <= 128 else _round_up(c, 128)
 
@@ -421,15 +422,16 @@ def conv1x1_int4_int8(x: torch.Tensor, w_packed: torch.Tensor, a_scale: float, w
     out = torch.empty((n, o, ho, wo), dtype=torch.float16 if output_half else torch.float32, device=x.device)
     if out.numel() == 0:
         return out
-    cp = conv_channels_padded(c)
-    xq = quantize_nchw_to_nhwc(x, a_scale, qn, qp, cp)
     if stride_h == stride_w and stride_h in (1, 2):
         stride = stride_h
     else:
-        xq = xq[:, ::stride_h, ::stride_w, :].contiguous()
         stride = 1
+    cp = conv_channels_padded(c, stride)
+    xq = quantize_nchw_to_nhwc(x, a_scale, qn, qp, cp)
+    if not (stride_h == stride_w and stride_h in (1, 2)):
+        xq = xq[:, ::stride_h, ::stride_w, :].contiguous()
     wr = repack_oihw_int4(w_packed, c, 1, 1, cp)
-    geom = ConvGeom(n, xq.shape[1], xq.shape[2], cp, 1, 1, stride, 0, 0, ho, wo, o, LAYOUT_NCHW, 0)
+    geom = ConvGeom(n, xq.shape[1], xq.shape[2], cp, 1, 1, stride, 0, 0, ho, wo, o, LAYOUT_NCHW, 0)  # noqa: E501
     epi = make_epilogue(OUT_F16 if output_half else OUT_F32, alpha_scalar=_combined_scale(a_scale, w_scale),
                         beta=bias)
     return conv2d_nhwc(xq, wr, W_INT4, geom, epi, out)
@@ -453,7 +455,7 @@ def conv_nchw(x: torch.Tensor, w_conv: torch.Tensor, w_kind: int, c: int, kh: in
     out = torch.empty((n, o, ho, wo), dtype=out_dtype, device=x.device)
     if out.numel() == 0:
         return out
-    cp = conv_channels_padded(c)
+    cp = conv_channels_padded(c, stride)
     if pad_code_of_zero:
         xq, p = _quantize_conv_input(x, a_scale, qn, qp, cp, pad)
     else:

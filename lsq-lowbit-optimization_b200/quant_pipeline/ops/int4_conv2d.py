@@ -96,21 +96,27 @@ class Int4WeightInt8ActConv2d(nn.Module):
     def _kernel_supported(self) -> bool:
         kh, kw = self.kernel_size
         return (self.dilation == (1, 1) and self.stride[0] == self.stride[1] and self.stride[0] in (1, 2)
-                and self.padding[0] == self.padding[1] and kh * kw * min(ext.conv_channels_padded(self.in_channels), 128) <= 2048)
+                and self.padding[0] == self.padding[1]
+                and kh * kw * min(ext.conv_channels_padded(self.in_channels, self.stride[0]), 128) <= 2048)
 
     def _conv_weight(self) -> torch.Tensor:
         wp = self.weight_packed
         key = (wp.data_ptr(), wp._version, wp.device)
         if self._kernel_weight is None or self._kernel_weight[0] != key:
             kh, kw = self.kernel_size
-            cp = ext.conv_channels_padded(self.in_channels)
+            cp = ext.conv_channels_padded(self.in_channels, self.stride[0])
             self._kernel_weight = (key, ext.repack_oihw_int4(wp.contiguous(), self.in_channels, kh, kw, cp))
         return self._kernel_weight[1]
 
     def _alpha(self, device):
-        """Scalar alpha (float) or per-channel alpha tensor: float(s_a * s_w)."""
+        """Scalar alpha (float) or per-channel alpha tensor. The reference's
+        fused 3x3 / 1x1 ops form float(double(s_a) * double(s_w)) from the
+        host floats (csrc/int4_int8_kernels.cu:345, 472); its general path
+        multiplies the float32 buffers (int4_conv2d.py:192). Both are kept."""
         if not isinstance(self.w_scale_host, torch.Tensor):
-            return ext._combined_scale(self.a_scale_host, self.w_scale_host), None
+            if self.is_spatial_3x3 or self.is_pointwise:
+                return ext._combined_scale(self.a_scale_host, self.w_scale_host), None
+            return float(self.a_scale.to(torch.float32).cpu() * self.w_scale.to(torch.float32).cpu()), None
         key = (device, self.a_scale_host)
         if self._alpha_cache is None or self._alpha_cache[0] != key:
             a = (self.a_scale_host * self.w_scale_host.to(torch.float64)).to(torch.float32).to(device)

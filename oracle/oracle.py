@@ -155,15 +155,24 @@ def conv1x1(x, w_packed, a_scale, w_scale, qn, qp, stride_h, stride_w, bias=None
     return y.astype(np.float16) if output_half else np.ascontiguousarray(y)
 
 
+def buffer_scale(a_scale: float, w_scale: float) -> np.float32:
+    """a_scale * w_scale of the modules' float32 buffers, multiplied in
+    float32 (quant_pipeline/ops/int4_conv2d.py:192). Equal to
+    combined_scale whenever both scales are float32 values (as produced by
+    the adapter, lsq_adapter.py:124-125)."""
+    return np.float32(np.float32(a_scale) * np.float32(w_scale))
+
+
 def conv_unfold_path(x, w_int, a_scale, w_scale, qn, qp, stride, pad, bias=None, out_dtype=np.float32):
     """The module's general path (quant_pipeline/ops/int4_conv2d.py:171-201):
-    quantise, unfold, GEMM, y = acc * (s_a*s_w) + bias, NCHW."""
+    quantise, unfold, GEMM, y = acc * (s_a*s_w) + bias with the float32
+    buffer product, NCHW."""
     n = x.shape[0]
     o, c, kh, kw = w_int.shape
     q = quantize(x, a_scale, qn, qp)
     cols, ho, wo = unfold_nchw(q, kh, kw, stride, pad)
     acc = gemm_s32(cols, w_int.reshape(o, -1))
-    y = epilogue(acc, combined_scale(a_scale, w_scale), bias)
+    y = epilogue(acc, buffer_scale(a_scale, w_scale), bias)
     return np.ascontiguousarray(y.reshape(n, ho, wo, o).transpose(0, 3, 1, 2)).astype(out_dtype)
 
 

@@ -58,7 +58,6 @@ CONV_CASES = [
     (2, 14, 14, 256, 512, 1, 2, 0),
     (2, 9, 13, 32, 48, 1, 1, 0),
     (2, 11, 9, 96, 80, 3, 1, 1),
-    (2, 12, 10, 16, 32, 3, 2, 1),
 ]
 
 
@@ -75,13 +74,37 @@ def test_conv_nhwc_s32_bitexact(cuda, n, h, w, c, o, k, stride, pad):
     assert ext.device_error() == 0
 
 
-def test_conv_channel_rule(cuda):
-    """c = 48 splits a 32-byte K-step across taps: rejected, not miscomputed."""
+@pytest.mark.parametrize("c,stride", [(48, 1), (16, 2)])
+def test_conv_channel_rule(cuda, c, stride):
+    """c = 48, or c = 16 at stride 2, would split a 32-byte K-step across
+    taps or stride phases: rejected on the host, not miscomputed."""
     g = rng(9)
-    xq = rand_i8(g, (1, 8, 8, 48), 0, 127)
-    wt = rand_i4(g, (16, 3, 3, 48))
+    xq = rand_i8(g, (1, 8, 8, c), 0, 127)
+    wt = rand_i4(g, (16, 3, 3, c))
+    ho = (8 + 2 - 3) // stride + 1
     with pytest.raises(RuntimeError, match="status 3"):
-        run_nhwc_conv(cuda, xq, wt, 1, 1, 8, 8, {}, ext.OUT_S32)
+        run_nhwc_conv(cuda, xq, wt, stride, 1, ho, ho, {}, ext.OUT_S32)
+
+
+def test_module_matches_reference_golden(cuda):
+    """Int4WeightInt8ActConv2d general-path geometries vs outputs of the
+    reference module itself (tests/golden/conv_paths.npz)."""
+    from pathlib import Path
+    from quant_pipeline.ops import Int4WeightInt8ActConv2d
+
+    d = np.load(Path(__file__).resolve().parent / "golden" / "conv_paths.npz")
+    cases = {"k3s2": (16, 32, 3, 2, 1), "k1s2": (16, 32, 1, 2, 0), "k7s2": (3, 16, 7, 2, 3), "k5s1": (3, 8, 5, 1, 2)}
+    for name, (cin, cout, k, s, p) in cases.items():
+        m = Int4WeightInt8ActConv2d(cin, cout, (k, k), (s, s), (p, p), (1, 1), 1, 0.0123, 0.05, -128, 127,
+                                    out_dtype=torch.float32, bias=True)
+        m.load_int4_weight(torch.from_numpy(d[f"{name}_w"]))
+        with torch.no_grad():
+            m.bias.copy_(torch.from_numpy(d[f"{name}_bias"]))
+        assert np.array_equal(m.weight_packed.numpy(), d[f"{name}_packed"])
+        m = m.to(cuda)
+        with torch.no_grad():
+            y = m(to_dev(d[f"{name}_x"], cuda))
+        assert_equal(y, d[f"{name}_y"], f"module {name} vs reference")
 
 
 def test_stem_s2d_conv(cuda):
