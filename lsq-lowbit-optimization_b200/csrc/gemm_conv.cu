@@ -141,18 +141,20 @@ extern "C" int w4a8_gemm(const int8_t* A, int64_t lda, const void* W, int64_t ld
   p.num_kb = (K + kBK - 1) / kBK;
   p.tiles_m = tiles_m;
   p.tiles_n = (N + bn - 1) / bn;
+  // Packed int4 weights land in the upper half of the int8 B stage and are
+  // expanded in place, so a stage is A (16 KB) + B (bn x 128 B).
   p.a_stage_bytes = kBM * kBK;
   p.b_stage_bytes = bn * kBK;
-  p.bp_stage_bytes = i4 ? bn * kBK / 2 : 0;
-  const uint32_t per_stage = p.a_stage_bytes + p.b_stage_bytes + p.bp_stage_bytes;
+  p.bp_stage_bytes = 0;
+  const uint32_t per_stage = p.a_stage_bytes + p.b_stage_bytes;
   p.stages = pick_stages(per_stage, 0);
   if (p.stages < 2) return W4A8_ERR_UNSUPPORTED;
   p.halo_stages = 0;
   p.a_off = 0;
   p.b_off = p.a_off + p.stages * p.a_stage_bytes;
-  p.bp_off = p.b_off + p.stages * p.b_stage_bytes;
-  p.h_off = p.bp_off + p.stages * p.bp_stage_bytes;
-  p.tx_bytes = p.a_stage_bytes + (i4 ? p.bp_stage_bytes : p.b_stage_bytes);
+  p.bp_off = 0;
+  p.h_off = p.b_off + p.stages * p.b_stage_bytes;
+  p.tx_bytes = p.a_stage_bytes + (i4 ? p.b_stage_bytes / 2 : p.b_stage_bytes);
   p.tmem_cols = 2 * bn < 32 ? 32 : 2 * bn;
   p.err = device_error_word();
   if (!p.err) return W4A8_ERR_LAUNCH;
@@ -297,8 +299,8 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   p.tiles_n = (g->o + bn - 1) / bn;
   p.a_stage_bytes = 0;
   p.b_stage_bytes = bn * kBK;
-  p.bp_stage_bytes = i4 ? bn * kBK / 2 : 0;
-  const uint32_t per_stage = p.b_stage_bytes + p.bp_stage_bytes;
+  p.bp_stage_bytes = 0;
+  const uint32_t per_stage = p.b_stage_bytes;
   p.halo_stages = 2;
   p.stages = pick_stages(per_stage, 2 * cp.halo_bytes);
   if (p.stages < 3) {
@@ -309,8 +311,8 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   p.a_off = 0;
   p.h_off = 0;
   p.b_off = p.halo_stages * cp.halo_bytes;
-  p.bp_off = p.b_off + p.stages * p.b_stage_bytes;
-  p.tx_bytes = i4 ? p.bp_stage_bytes : p.b_stage_bytes;
+  p.bp_off = 0;
+  p.tx_bytes = i4 ? p.b_stage_bytes / 2 : p.b_stage_bytes;
   p.tmem_cols = 2 * bn;
   p.err = device_error_word();
   if (!p.err) return W4A8_ERR_LAUNCH;

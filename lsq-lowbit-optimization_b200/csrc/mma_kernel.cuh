@@ -6,11 +6,14 @@
 // Rows of A are GEMM rows (GEMM mode) or a 16x8 block of output pixels of
 // one image (conv mode); columns are output features / channels.
 //
-// Warp roles (384 threads):
-//   warp 0      TMA producer (one elected lane)
-//   warp 1      TMEM owner + MMA issuer (one elected lane)
-//   warps 4-7   epilogue: tcgen05.ld -> fused LSQ epilogue -> global stores
-//   warps 8-11  int4 unpack: packed nibbles (smem, TMA) -> int8 SW128 tile
+// Warp roles (512 threads):
+//   warp 0       TMA producer (one elected lane)
+//   warp 1       TMEM owner + MMA issuer (one elected lane)
+//   warps 4-11   epilogue: tcgen05.ld -> fused LSQ epilogue -> global stores;
+//                warp w reads TMEM lanes 32*(w%4).. and column half (w-4)/4
+//   warps 12-15  int4 unpack: the packed nibbles land (TMA) in the upper half
+//                of the int8 B stage and are expanded in place into the
+//                128B-swizzled int8 tile
 // The accumulator is double-buffered in TMEM so the epilogue of tile i
 // overlaps the main loop of tile i+1.
 #pragma once
@@ -23,7 +26,9 @@ namespace w4a8 {
 
 constexpr int kBM = 128;          // rows per tile (MMA M)
 constexpr int kBK = 128;          // K bytes per k-block (one 128B swizzle atom)
-constexpr int kThreads = 384;
+constexpr int kThreads = 512;
+constexpr int kEpiWarps = 8;      // warps 4..11
+constexpr int kUnpackWarp0 = 12;  // warps 12..15
 constexpr int kMaxStages = 8;
 constexpr int kMaxHaloStages = 2;
 constexpr int kMaxSteps = 64;     // conv MMA K-steps (32 B) per channel group
@@ -79,79 +84,154 @@ struct KParams {
 };
 
 // ----------------------------- epilogue ------------------------------------
-__device__ __forceinline__ void store16_f32(float* dst, const float (&v)[16], int ncols, long long s_ch) {
-  if (ncols == 16 && s_ch == 1 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-    float4* d4 = reinterpret_cast<float4*>(dst);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-  } else {
-    for (int i = 0; i < ncols; ++i) dst[i * s_ch] = v[i];
-  }
+// Exact int32 -> float32 (round to nearest even) without the conversion
+// unit for |a| < 2^22: 1.5*2^23 + a is exact in float32, then subtract.
+__device__ __forceinline__ float i2f_exact(int a) {
+  if (__builtin_expect(static_cast<unsigned>(a + 0x400000) < 0x800000u, 1))
+    return __fsub_rn(__int_as_float(a + 0x4B400000), 12582912.0f);
+  return __int2float_rn(a);
 }
 
-__device__ __forceinline__ void epilogue_chunk(const EpiParams& e, const uint32_t (&acc)[16], int n, long long out_off,
-                                               long long prow) {
+// LSQ code clamp(rint(y / s), qn, qp) with IEEE division semantics.
+// t = fl(y * fl(1/s)) differs from fl(y/s) by at most |y/s| * 3.1 * 2^-24
+// (< 6.1e-5 for |t| < 256), so rint(t) == rint(fl(y/s)) unless t lies
+// within that distance of a half-integer; inside a 2^-12 guard band the
+// exact quotient is computed. |t| >= 256 always clamps. The final float ->
+// int uses 1.5*2^23 (round to nearest even, exact after the clamp).
+__device__ __forceinline__ int lsq_code(float y, float s, float rs, float qnf, float qpf) {
+  float t = __fmul_rn(y, rs);
+  if (fabsf(t) < 256.0f) {
+    const float rt = __fsub_rn(__fadd_rn(t, 12582912.0f), 12582912.0f);
+    if (fabsf(fabsf(__fsub_rn(t, rt)) - 0.5f) < 2.44140625e-4f) t = __fdiv_rn(y, s);
+  }
+  t = fminf(fmaxf(t, qnf), qpf);
+  return __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
+}
+
+struct EpiConsts {
+  float rs, qnf, qpf;
+};
+
+// Applies the fused epilogue to 16 accumulators (columns n .. n+15) of one
+// output row; all indexing is static so nothing spills to local memory.
+__device__ __forceinline__ void epilogue16(const EpiParams& e, const EpiConsts& k, const uint32_t* acc, int n,
+                                           long long out_off, long long prow) {
   const int ncols = min(16, e.n_total - n);
   if (ncols <= 0) return;
+  const bool vec = (ncols == 16) && (e.s_ch == 1);
   if (e.out_kind == 0) {
     int32_t* dst = static_cast<int32_t*>(e.out) + out_off;
-    if (ncols == 16 && e.s_ch == 1 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-      int4* d4 = reinterpret_cast<int4*>(dst);
+    if (vec && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        d4[i] = make_int4(int(acc[4 * i]), int(acc[4 * i + 1]), int(acc[4 * i + 2]), int(acc[4 * i + 3]));
+        reinterpret_cast<int4*>(dst)[i] =
+            make_int4(int(acc[4 * i]), int(acc[4 * i + 1]), int(acc[4 * i + 2]), int(acc[4 * i + 3]));
     } else {
-      for (int i = 0; i < ncols; ++i) dst[i * e.s_ch] = int(acc[i]);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < ncols) dst[i * e.s_ch] = int(acc[i]);
     }
     return;
   }
-  float y[16];
-  const float* res = e.residual ? e.residual + prow * e.res_ld + n : nullptr;
+  float a[16], b[16], y[16];
+  if (ncols == 16 && e.alpha && (reinterpret_cast<uintptr_t>(e.alpha + n) & 15) == 0) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    if (i < ncols) {
-      const float a = e.alpha ? __ldg(e.alpha + n + i) : e.alpha_scalar;
-      float v = __fmul_rn(__int2float_rn(int(acc[i])), a);
-      if (e.beta) v = __fadd_rn(v, __ldg(e.beta + n + i));
-      if (res) v = __fadd_rn(v, res[i]);
-      if (e.relu) v = fmaxf(v, 0.0f);
-      y[i] = v;
+    for (int i = 0; i < 4; ++i) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(e.alpha + n) + i);
+      a[4 * i] = v.x; a[4 * i + 1] = v.y; a[4 * i + 2] = v.z; a[4 * i + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) a[i] = (e.alpha && i < ncols) ? __ldg(e.alpha + n + i) : e.alpha_scalar;
+  }
+  if (e.beta) {
+    if (ncols == 16 && (reinterpret_cast<uintptr_t>(e.beta + n) & 15) == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(e.beta + n) + i);
+        b[4 * i] = v.x; b[4 * i + 1] = v.y; b[4 * i + 2] = v.z; b[4 * i + 3] = v.w;
+      }
     } else {
-      y[i] = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) b[i] = i < ncols ? __ldg(e.beta + n + i) : 0.0f;
     }
   }
-  if (e.aux) store16_f32(e.aux + prow * e.aux_ld + n, y, ncols, 1);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    y[i] = __fmul_rn(i2f_exact(int(acc[i])), a[i]);
+    if (e.beta) y[i] = __fadd_rn(y[i], b[i]);
+  }
+  if (e.residual) {
+    const float* res = e.residual + prow * e.res_ld + n;
+    if (ncols == 16 && (reinterpret_cast<uintptr_t>(res) & 15) == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 v = *reinterpret_cast<const float4*>(res + 4 * i);
+        y[4 * i] = __fadd_rn(y[4 * i], v.x);
+        y[4 * i + 1] = __fadd_rn(y[4 * i + 1], v.y);
+        y[4 * i + 2] = __fadd_rn(y[4 * i + 2], v.z);
+        y[4 * i + 3] = __fadd_rn(y[4 * i + 3], v.w);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < ncols) y[i] = __fadd_rn(y[i], res[i]);
+    }
+  }
+  if (e.relu) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) y[i] = fmaxf(y[i], 0.0f);
+  }
+  if (e.aux) {
+    float* dst = e.aux + prow * e.aux_ld + n;
+    if (ncols == 16 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        reinterpret_cast<float4*>(dst)[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < ncols) dst[i] = y[i];
+    }
+  }
   if (e.out_kind == 1) {
-    store16_f32(static_cast<float*>(e.out) + out_off, y, ncols, e.s_ch);
+    float* dst = static_cast<float*>(e.out) + out_off;
+    if (vec && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        reinterpret_cast<float4*>(dst)[i] = make_float4(y[4 * i], y[4 * i + 1], y[4 * i + 2], y[4 * i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < ncols) dst[i * e.s_ch] = y[i];
+    }
   } else if (e.out_kind == 2) {
     __half* dst = static_cast<__half*>(e.out) + out_off;
-    if (ncols == 16 && e.s_ch == 1 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    if (vec && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
       uint32_t w[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const __half lo = __float2half_rn(y[2 * i]);
-        const __half hi = __float2half_rn(y[2 * i + 1]);
-        w[i] = uint32_t(__half_as_ushort(lo)) | (uint32_t(__half_as_ushort(hi)) << 16);
-      }
-      uint4* d4 = reinterpret_cast<uint4*>(dst);
-      d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
-      d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      for (int i = 0; i < 8; ++i)
+        w[i] = uint32_t(__half_as_ushort(__float2half_rn(y[2 * i]))) |
+               (uint32_t(__half_as_ushort(__float2half_rn(y[2 * i + 1]))) << 16);
+      reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
     } else {
-      for (int i = 0; i < ncols; ++i) dst[i * e.s_ch] = __float2half_rn(y[i]);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < ncols) dst[i * e.s_ch] = __float2half_rn(y[i]);
     }
   } else {
     int8_t* dst = static_cast<int8_t*>(e.out) + out_off;
-    uint32_t w[4] = {0, 0, 0, 0};
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      int q = __float2int_rn(__fdiv_rn(y[i], e.out_scale));
-      q = max(e.qn, min(e.qp, q));
-      w[i >> 2] |= (uint32_t(q) & 0xFFu) << (8 * (i & 3));
-    }
-    if (ncols == 16 && e.s_ch == 1 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+    for (int i = 0; i < 16; ++i)
+      w[i >> 2] |= (uint32_t(lsq_code(y[i], e.out_scale, k.rs, k.qnf, k.qpf)) & 0xFFu) << (8 * (i & 3));
+    if (vec && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
       *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
     } else {
-      for (int i = 0; i < ncols; ++i) dst[i * e.s_ch] = int8_t((w[i >> 2] >> (8 * (i & 3))) & 0xFFu);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < ncols) dst[i * e.s_ch] = int8_t((w[i >> 2] >> (8 * (i & 3))) & 0xFFu);
     }
   }
 }
@@ -217,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bar_tfull[b], 1);
-      mbar_init(&bar_tempty[b], 128);
+      mbar_init(&bar_tempty[b], kEpiWarps * 32);
     }
     mbar_init(&bar_drain, 1);
     abort_flag = 0;
@@ -227,9 +307,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmW);
     if constexpr (!kConv) tma_prefetch_desc(&tmA);
   }
-  if (kConv && threadIdx.x >= 32 && threadIdx.x < 64) {
-    // Zero the halo buffers once: rows a sub-tile box does not cover stay 0.
-    for (uint32_t i = (threadIdx.x - 32) * 16; i < p.conv.halo_bytes * p.halo_stages; i += 32 * 16)
+  if (kConv && warp == 2) {
+    // Zero the halo buffers once: bytes no box covers stay 0.
+    for (uint32_t i = lane * 16; i < p.conv.halo_bytes * p.halo_stages; i += 32 * 16)
       *reinterpret_cast<uint4*>(base + p.h_off + i) = make_uint4(0, 0, 0, 0);
     fence_proxy_async_smem();
   }
@@ -263,10 +343,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           oh0 = th * kTileH;
           ow0 = (rem - th * p.conv.tiles_w) * kTileW;
         }
+        int g = 0, kb_in_g = 0;
         for (int kb = 0; ok && kb < p.num_kb; ++kb) {
           if constexpr (kConv) {
-            if (kb % kbpg == 0) {
-              const int g = kb / kbpg;
+            if (kb_in_g == 0) {
               if (!mbar_wait(&bar_hempty[hs], hph ^ 1, &abort_flag)) { ok = false; break; }
               mbar_arrive_expect_tx(&bar_hfull[hs], p.conv.halo_tx_bytes);
               uint8_t* hdst = base + p.h_off + hs * p.conv.halo_bytes;
@@ -281,12 +361,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (!mbar_wait(&bar_empty[s], ph ^ 1, &abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&bar_full[s], p.tx_bytes);
-          if constexpr (!kConv) tma_load_2d(base + p.a_off + s * p.a_stage_bytes, &tmA, &bar_full[s], kb * kBK, mt * kBM);
+          if constexpr (!kConv)
+            tma_load_2d(base + p.a_off + s * p.a_stage_bytes, &tmA, &bar_full[s], kb * kBK, mt * kBM);
+          uint8_t* bdst = base + p.b_off + s * p.b_stage_bytes;
           if constexpr (kInt4)
-            tma_load_2d(base + p.bp_off + s * p.bp_stage_bytes, &tmW, &bar_full[s], kb * (kBK / 2), nt * BN);
+            tma_load_2d(bdst + BN * (kBK / 2), &tmW, &bar_full[s], kb * (kBK / 2), nt * BN);
           else
-            tma_load_2d(base + p.b_off + s * p.b_stage_bytes, &tmW, &bar_full[s], kb * kBK, nt * BN);
+            tma_load_2d(bdst, &tmW, &bar_full[s], kb * kBK, nt * BN);
           if (++s == p.stages) { s = 0; ph ^= 1; }
+          if (kConv && ++kb_in_g == kbpg) { kb_in_g = 0; ++g; }
         }
       }
       // Drain: every TMA this thread issued has landed before the CTA exits.
@@ -319,9 +402,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         uint32_t halo_addr = 0;
+        int kb_in_g = 0;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if constexpr (kConv) {
-            if (kb % kbpg == 0) {
+            if (kb_in_g == 0) {
               if (!mbar_wait(&bar_hfull[hs], hph, &abort_flag)) { ok = false; break; }
               halo_addr = base_u32 + p.h_off + hs * p.conv.halo_bytes;
             }
@@ -333,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < kBK / 32; ++j) {
             uint64_t a_desc;
             if constexpr (kConv) {
-              const int step = (kb % kbpg) * 4 + j;
+              const int step = kb_in_g * 4 + j;
               a_desc = make_smem_desc(halo_addr + p.conv.step_off[step], p.conv.step_lbo[step],
                                       p.conv.halo_w * 16, kLayoutNone);
             } else {
@@ -344,7 +428,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           mma_commit(&bar_empty[s]);
           if constexpr (kConv) {
-            if (kb % kbpg == kbpg - 1) {
+            if (++kb_in_g == kbpg) {
+              kb_in_g = 0;
               mma_commit(&bar_hempty[hs]);
               if (++hs == p.halo_stages) { hs = 0; hph ^= 1; }
             }
@@ -361,10 +446,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (global_timer_ns() - t0 > kWaitLimitNs) { atomicOr(p.err, kErrTimeoutDrain); break; }
       if (!ok) atomicOr(p.err, kErrTimeoutMma);
     }
-  } else if (warp >= 4 && warp < 8) {
+  } else if (warp >= 4 && warp < 4 + kEpiWarps) {
     // ----------------------------- epilogue --------------------------------
-    const int q = warp - 4;
+    const int q = warp & 3;
+    const int half = (warp - 4) >> 2;
     const int m = q * 32 + lane;
+    EpiConsts k;
+    k.rs = p.epi.out_kind == 3 ? __frcp_rn(p.epi.out_scale) : 1.0f;
+    k.qnf = float(p.epi.qn);
+    k.qpf = float(p.epi.qp);
     int it = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
       const int buf = it & 1;
@@ -382,36 +472,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool valid = row_coords<kConv>(p, mt, m, out_off, prow);
       const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + buf * BN;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t acc[16];
-        tmem_ld16(t_addr + c0, acc);
+      for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
+        uint32_t acc[32];
+        tmem_ld16(t_addr + c0, *reinterpret_cast<uint32_t(*)[16]>(acc));
+        tmem_ld16(t_addr + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(acc + 16));
         tmem_ld_wait();
-        const int n = nt * BN + c0;
-        if (valid) epilogue_chunk(p.epi, acc, n, out_off + (long long)n * p.epi.s_ch, prow);
+        if (valid) {
+          const int n = nt * BN + c0;
+          epilogue16(p.epi, k, acc, n, out_off + (long long)n * p.epi.s_ch, prow);
+          epilogue16(p.epi, k, acc + 16, n + 16, out_off + (long long)(n + 16) * p.epi.s_ch, prow);
+        }
       }
       tc_fence_before();
       mbar_arrive(&bar_tempty[buf]);
     }
-  } else if (warp >= 8 && kInt4) {
+  } else if (warp >= kUnpackWarp0 && kInt4) {
     // ------------------------------ unpack ---------------------------------
-    const int ut = threadIdx.x - 256;
+    // Phase 1 reads every packed chunk this thread owns into registers,
+    // a named barrier orders all reads before any write, phase 2 writes the
+    // int8 rows over the stage (the packed half is overwritten in place).
+    constexpr int kPer = BN * 8 / 128;
+    const int ut = threadIdx.x - kUnpackWarp0 * 32;
     int s = 0;
     uint32_t ph = 0;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
       for (int kb = 0; kb < p.num_kb; ++kb) {
-        if (!mbar_wait(&bar_full[s], ph, &abort_flag)) { ok = false; break; }
-        const uint8_t* src = base + p.bp_off + s * p.bp_stage_bytes;
-        uint8_t* dst = base + p.b_off + s * p.b_stage_bytes;
-#pragma unroll 4
-        for (int idx = ut; idx < BN * 8; idx += 128) {
-          const int r = idx >> 3;
-          const int c = idx & 7;
-          const uint2 v = *reinterpret_cast<const uint2*>(src + r * 64 + c * 8);
+        const bool got = mbar_wait(&bar_full[s], ph, &abort_flag);
+        if (!bar_and(1, 128, got)) { ok = false; break; }
+        uint8_t* stage = base + p.b_off + s * p.b_stage_bytes;
+        const uint8_t* src = stage + BN * (kBK / 2);
+        uint2 v[kPer];
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+          const int idx = ut + 128 * j;
+          v[j] = *reinterpret_cast<const uint2*>(src + (idx >> 3) * 64 + (idx & 7) * 8);
+        }
+        bar_sync(1, 128);
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+          const int idx = ut + 128 * j;
+          const int r = idx >> 3, c = idx & 7;
           uint4 o;
-          unpack_nibbles8(v.x, o.x, o.y);
-          unpack_nibbles8(v.y, o.z, o.w);
-          *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = o;
+          unpack_nibbles8(v[j].x, o.x, o.y);
+          unpack_nibbles8(v[j].y, o.z, o.w);
+          *reinterpret_cast<uint4*>(stage + r * 128 + ((c ^ (r & 7)) << 4)) = o;
         }
         fence_proxy_async_smem();
         mbar_arrive(&bar_ready[s]);

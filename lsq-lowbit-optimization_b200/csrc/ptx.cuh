@@ -86,6 +86,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// AND of `v` over the `count` threads meeting at named barrier `id`; every
+// participant gets the same answer, so a group can abort uniformly.
+__device__ __forceinline__ bool bar_and(uint32_t id, uint32_t count, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.and.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(v)), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void bar_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
