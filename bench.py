@@ -207,24 +207,34 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         if world > 1:
             gather_logits(logits, gathered)
 
-    def step_e2e():
-        engine.images.copy_(host_images, non_blocking=True)
-        logits = engine.forward()
-        if world > 1:
-            gather_logits(logits, gathered)
-        host_logits.copy_(logits, non_blocking=True)
+    post = (lambda logits: gather_logits(logits, gathered)) if world > 1 else None
+    copy_stream = torch.cuda.Stream(device)
+    outs = [torch.empty((B, classes), dtype=torch.float32).pin_memory() for _ in range(2)]
 
-    def timed(fn, steps: int) -> float:
-        for _ in range(args.warmup):
-            fn()
+    def run_e2e(steps: int):
+        """Public serving API over host buffers: every step uploads its
+        pinned fp32 images (overlapped with the previous batch's compute on
+        a copy stream), runs the forward and reads the logits back."""
+        engine.infer_host([host_images] * steps, out=[outs[i % 2] for i in range(steps)],
+                          copy_stream=copy_stream, post=post)
+
+    def timed(fn, steps: int, warm=None) -> float:
+        if warm is not None:
+            warm()
+        else:
+            for _ in range(args.warmup):
+                fn()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
-        for _ in range(steps):
-            fn()
+        if warm is not None:
+            fn(steps)
+        else:
+            for _ in range(steps):
+                fn()
         e.record()
         torch.cuda.synchronize()
         if world > 1:
@@ -238,7 +248,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     sampler = ClockSampler(local_rank).start() if rank == 0 else None
     total_ms = timed(step, args.steps)
     clocks = sampler.stop() if sampler else None
-    e2e_ms = timed(step_e2e, args.steps)
+    e2e_ms = timed(run_e2e, args.steps, warm=lambda: run_e2e(args.warmup))
     if ext.device_error():
         raise RuntimeError("a kernel recorded a device-side wait timeout")
 
@@ -259,7 +269,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
                        "timing": "CUDA graph replay of the whole forward (+ NCCL all-gather of logits when N>1)"},
             "gpu_launches": engine.launches * args.steps,
             "e2e": {"value": B * world / (e2e_ms / args.steps * 1e-3), "unit": "images/s",
-                    "h2d_bytes_per_step": host_images.numel() * 4, "d2h_bytes_per_step": host_logits.numel() * 4},
+                    "h2d_bytes_per_step": host_images.numel() * 4, "d2h_bytes_per_step": host_logits.numel() * 4,
+                    "api": "W4A8ResNetEngine.infer_host (pinned host images in, host logits out; upload of "
+                           "batch i+1 overlapped with batch i on a copy stream)"},
             "clocks": clocks,
         }
         if not args.no_extras and world == 1:

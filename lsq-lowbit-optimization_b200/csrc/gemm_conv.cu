@@ -301,13 +301,26 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   p.b_stage_bytes = bn * kBK;
   p.bp_stage_bytes = 0;
   const uint32_t per_stage = p.b_stage_bytes;
-  p.halo_stages = 2;
-  p.stages = pick_stages(per_stage, 2 * cp.halo_bytes);
-  if (p.stages < 3) {
-    p.halo_stages = 1;
-    p.stages = pick_stages(per_stage, cp.halo_bytes);
+  // Resident weights: with a single n-tile and all k-blocks fitting next to
+  // at least two halo stages, the CTA loads and unpacks the weights once and
+  // then streams only input halos.
+  const uint32_t bres_bytes = uint32_t(p.num_kb) * per_stage;
+  p.b_resident = 0;
+  if (p.tiles_n == 1 && bres_bytes + 2 * cp.halo_bytes <= uint32_t(kSmemBudget)) {
+    p.b_resident = 1;
+    p.stages = 1;
+    p.halo_stages = std::min<int>(kMaxHaloStages, (kSmemBudget - bres_bytes) / cp.halo_bytes);
+    p.bres_tx_bytes = i4 ? bres_bytes / 2 : bres_bytes;
+  } else {
+    // Deepest halo pipeline (each stage is one tile's input window) that
+    // still leaves at least three weight stages.
+    p.stages = 0;
+    for (int hs = kMaxHaloStages; hs >= 1 && p.stages < 3; --hs) {
+      p.halo_stages = hs;
+      p.stages = pick_stages(per_stage, hs * cp.halo_bytes);
+    }
+    if (p.stages < 2) return W4A8_ERR_UNSUPPORTED;
   }
-  if (p.stages < 2) return W4A8_ERR_UNSUPPORTED;
   p.a_off = 0;
   p.h_off = 0;
   p.b_off = p.halo_stages * cp.halo_bytes;

@@ -30,7 +30,7 @@ constexpr int kThreads = 512;
 constexpr int kEpiWarps = 8;      // warps 4..11
 constexpr int kUnpackWarp0 = 12;  // warps 12..15
 constexpr int kMaxStages = 8;
-constexpr int kMaxHaloStages = 2;
+constexpr int kMaxHaloStages = 6;
 constexpr int kMaxSteps = 64;     // conv MMA K-steps (32 B) per channel group
 constexpr int kTileH = 16;        // conv: output rows per tile (one 8-row core group each)
 constexpr int kTileW = 8;         // conv: output columns per tile
@@ -77,6 +77,8 @@ struct KParams {
   uint32_t a_off, b_off, bp_off, h_off;  // smem region offsets (from 1024-aligned base)
   uint32_t a_stage_bytes, b_stage_bytes, bp_stage_bytes;
   uint32_t tx_bytes;  // TMA bytes per operand stage
+  int b_resident;     // conv, one n-tile: all weight k-blocks stay in smem
+  uint32_t bres_tx_bytes;
   uint32_t tmem_cols;
   unsigned* err;
   EpiParams epi;
@@ -106,6 +108,16 @@ __device__ __forceinline__ int lsq_code(float y, float s, float rs, float qnf, f
   }
   t = fminf(fmaxf(t, qnf), qpf);
   return __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
+}
+
+// Guard-band fix-up of one fast quotient t = fl(y * fl(1/s)): returns the
+// exact fl(y / s) when t is within 2^-12 of a half-integer, else t.
+__device__ __forceinline__ float lsq_guard(float y, float t, float s) {
+  if (fabsf(t) < 256.0f) {
+    const float rt = __fsub_rn(__fadd_rn(t, 12582912.0f), 12582912.0f);
+    if (fabsf(fabsf(__fsub_rn(t, rt)) - 0.5f) < 2.44140625e-4f) return __fdiv_rn(y, s);
+  }
+  return t;
 }
 
 struct EpiConsts {
@@ -156,9 +168,21 @@ __device__ __forceinline__ void epilogue16(const EpiParams& e, const EpiConsts& 
       for (int i = 0; i < 16; ++i) b[i] = i < ncols ? __ldg(e.beta + n + i) : 0.0f;
     }
   }
+  // int32 -> float32: exact add-and-subtract of 1.5*2^23 unless a value
+  // needs more than 22 bits (checked once for all 16).
+  uint32_t oor = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) oor |= (acc[i] + 0x400000u) & 0xFF800000u;
+  if (oor == 0) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) y[i] = __fsub_rn(__int_as_float(int(acc[i]) + 0x4B400000), 12582912.0f);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) y[i] = __int2float_rn(int(acc[i]));
+  }
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    y[i] = __fmul_rn(i2f_exact(int(acc[i])), a[i]);
+    y[i] = __fmul_rn(y[i], a[i]);
     if (e.beta) y[i] = __fadd_rn(y[i], b[i]);
   }
   if (e.residual) {
@@ -222,10 +246,27 @@ __device__ __forceinline__ void epilogue16(const EpiParams& e, const EpiConsts& 
     }
   } else {
     int8_t* dst = static_cast<int8_t*>(e.out) + out_off;
+    // Codes clamp(rint(y / s)): multiply by fl(1/s); the exact quotient is
+    // taken only for values inside the rounding guard band (see lsq_code),
+    // decided for all 16 at once so the common path has no branches.
+    float t[16];
+    bool slow = false;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      t[i] = __fmul_rn(y[i], k.rs);
+      const float rt = __fsub_rn(__fadd_rn(t[i], 12582912.0f), 12582912.0f);
+      slow |= (fabsf(t[i]) < 256.0f) & (fabsf(fabsf(__fsub_rn(t[i], rt)) - 0.5f) < 2.44140625e-4f);
+    }
+    if (slow) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) t[i] = lsq_guard(y[i], t[i], e.out_scale);
+    }
     uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
-      w[i >> 2] |= (uint32_t(lsq_code(y[i], e.out_scale, k.rs, k.qnf, k.qpf)) & 0xFFu) << (8 * (i & 3));
+    for (int i = 0; i < 16; ++i) {
+      const float c = fminf(fmaxf(t[i], k.qnf), k.qpf);
+      w[i >> 2] |= (uint32_t(__float_as_int(__fadd_rn(c, 12582912.0f)) - 0x4B400000) & 0xFFu) << (8 * (i & 3));
+    }
     if (vec && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
       *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
     } else {
@@ -277,6 +318,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t bar_tfull[2];
   __shared__ __align__(8) uint64_t bar_tempty[2];
   __shared__ __align__(8) uint64_t bar_drain;
+  __shared__ __align__(8) uint64_t bar_bres;    // resident weights landed
+  __shared__ __align__(8) uint64_t bar_bready;  // resident weights unpacked
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
 
@@ -300,6 +343,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar_tempty[b], kEpiWarps * 32);
     }
     mbar_init(&bar_drain, 1);
+    mbar_init(&bar_bres, 1);
+    mbar_init(&bar_bready, 128);
     abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -331,6 +376,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0, hs = 0;
       uint32_t ph = 0, hph = 0;
       bool ok = true;
+      if (kConv && p.b_resident) {
+        mbar_arrive_expect_tx(&bar_bres, p.bres_tx_bytes);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          uint8_t* bdst = base + p.b_off + kb * p.b_stage_bytes;
+          if constexpr (kInt4)
+            tma_load_2d(bdst + BN * (kBK / 2), &tmW, &bar_bres, kb * (kBK / 2), 0);
+          else
+            tma_load_2d(bdst, &tmW, &bar_bres, kb * kBK, 0);
+        }
+      }
       for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
         const int mt = t / p.tiles_n;
         const int nt = t - mt * p.tiles_n;
@@ -359,6 +414,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (++hs == p.halo_stages) { hs = 0; hph ^= 1; }
             }
           }
+          if (kConv && p.b_resident) {
+            if (++kb_in_g == kbpg) { kb_in_g = 0; ++g; }
+            continue;
+          }
           if (!mbar_wait(&bar_empty[s], ph ^ 1, &abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&bar_full[s], p.tx_bytes);
           if constexpr (!kConv)
@@ -380,6 +439,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         while (!mbar_try_wait(&bar_full[idx], par))
           if (global_timer_ns() - t0 > kWaitLimitNs) { abort_flag = 1; break; }
       }
+      if (kConv && p.b_resident) {
+        const unsigned long long t0 = global_timer_ns();
+        while (!mbar_try_wait(&bar_bres, 0))
+          if (global_timer_ns() - t0 > kWaitLimitNs) { abort_flag = 1; break; }
+      }
       for (int i = 0; kConv && i < p.halo_stages; ++i) {
         const int idx = (hs + p.halo_stages - 1 - i) % p.halo_stages;
         const uint32_t par = (idx < hs) ? hph : (hph ^ 1);
@@ -396,6 +460,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int s = 0, hs = 0, it = 0;
       uint32_t ph = 0, hph = 0;
       bool ok = true;
+      const bool resident = kConv && p.b_resident;
+      if (resident) ok = mbar_wait(kInt4 ? &bar_bready : &bar_bres, 0, &abort_flag);
       for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x, ++it) {
         const int buf = it & 1;
         if (!mbar_wait(&bar_tempty[buf], ((it >> 1) & 1) ^ 1, &abort_flag)) { ok = false; break; }
@@ -410,9 +476,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               halo_addr = base_u32 + p.h_off + hs * p.conv.halo_bytes;
             }
           }
-          if (!mbar_wait(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag)) { ok = false; break; }
+          if (!resident) {
+            if (!mbar_wait(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag)) { ok = false; break; }
+          }
           tc_fence_after();
-          const uint32_t b_addr = base_u32 + p.b_off + s * p.b_stage_bytes;
+          const uint32_t b_addr = base_u32 + p.b_off + (resident ? kb : s) * p.b_stage_bytes;
 #pragma unroll
           for (int j = 0; j < kBK / 32; ++j) {
             uint64_t a_desc;
@@ -426,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t b_desc = make_smem_desc(b_addr + j * 32, 16, 1024, kLayoutSw128);
             mma_i8_ss(d_tmem, a_desc, b_desc, idesc, (kb | j) != 0 ? 1u : 0u);
           }
-          mma_commit(&bar_empty[s]);
+          if (!resident) mma_commit(&bar_empty[s]);
           if constexpr (kConv) {
             if (++kb_in_g == kbpg) {
               kb_in_g = 0;
@@ -434,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (++hs == p.halo_stages) { hs = 0; hph ^= 1; }
             }
           }
-          if (++s == p.stages) { s = 0; ph ^= 1; }
+          if (!resident && ++s == p.stages) { s = 0; ph ^= 1; }
         }
         if (!ok) break;
         mma_commit(&bar_tfull[buf]);
@@ -496,11 +564,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     int s = 0;
     uint32_t ph = 0;
     bool ok = true;
-    for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+    const bool resident = kConv && p.b_resident;
+    if (resident) ok = bar_and(1, 128, mbar_wait(&bar_bres, 0, &abort_flag));
+    const int passes = resident ? 1 : total_tiles;  // resident weights: one pass over the k-blocks
+    for (int t = resident ? 0 : int(blockIdx.x); ok && t < passes; t += resident ? 1 : int(gridDim.x)) {
       for (int kb = 0; kb < p.num_kb; ++kb) {
-        const bool got = mbar_wait(&bar_full[s], ph, &abort_flag);
-        if (!bar_and(1, 128, got)) { ok = false; break; }
-        uint8_t* stage = base + p.b_off + s * p.b_stage_bytes;
+        if (!resident) {
+          const bool got = mbar_wait(&bar_full[s], ph, &abort_flag);
+          if (!bar_and(1, 128, got)) { ok = false; break; }
+        }
+        uint8_t* stage = base + p.b_off + (resident ? kb : s) * p.b_stage_bytes;
         const uint8_t* src = stage + BN * (kBK / 2);
         uint2 v[kPer];
 #pragma unroll
@@ -519,10 +592,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint4*>(stage + r * 128 + ((c ^ (r & 7)) << 4)) = o;
         }
         fence_proxy_async_smem();
+        if (resident) {
+          bar_sync(1, 128);  // the next k-block's reads follow this one's writes
+          continue;
+        }
         mbar_arrive(&bar_ready[s]);
         if (++s == p.stages) { s = 0; ph ^= 1; }
       }
     }
+    if (resident && ok) mbar_arrive(&bar_bready);
     if (!ok && ut == 0) atomicOr(p.err, kErrTimeoutUnpack);
   }
 

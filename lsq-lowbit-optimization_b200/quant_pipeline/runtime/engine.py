@@ -161,6 +161,7 @@ class W4A8ResNetEngine:
         self._keep: list = []
         self.use_graph = use_graph
         self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.graphs: List[torch.cuda.CUDAGraph] = []
         with torch.cuda.device(self.device):
             self._build(model, image_hw)
 
@@ -247,11 +248,24 @@ class W4A8ResNetEngine:
 
         # Stem: s2d + quantise -> 4x4 conv (W8) -> f32 -> maxpool -> f32 + codes.
         s_a, qn, qp = stem.qin
-        self.images = self._buf((B, 3, image_hw, image_hw), torch.float32)
+        # Two input slots: a graph is captured per slot so the next batch can
+        # be uploaded into one slot while the other is being consumed.
+        self.inputs = [self._buf((B, 3, image_hw, image_hw), torch.float32) for _ in range(2)]
+        self.images = self.inputs[0]
+        self._slot = 0
         h2 = image_hw // 2
         s2d = self._buf((B, h2, h2, 16), torch.int8)
-        self._add(self.lib.w4a8_s2d_quantize, (self.images.data_ptr(), s2d.data_ptr(), B, 3, image_hw, image_hw,
-                                               16, s_a, qn, qp), "s2d")
+        s2d_args = (s2d.data_ptr(), B, 3, image_hw, image_hw, 16, s_a, qn, qp)
+        self._keep.append(s2d_args)
+
+        def s2d_step(stream: int, fn=self.lib.w4a8_s2d_quantize, args=s2d_args) -> None:
+            rc = fn(self.inputs[self._slot].data_ptr(), *args, stream)
+            if rc != 0:
+                raise RuntimeError(f"s2d failed: libw4a8 status {rc}")
+
+        self.steps.append(s2d_step)
+        self.meta.append({"name": "s2d", "ops": 0.0, "bytes": float(B * 3 * image_hw * image_hw * 4 + s2d.numel())})
+        self.launches += 1
         stem4 = ConvSpec(stem_s2d_weights(stem.w_codes), stem.w_bits, 1, 2, stem.qin, stem.alpha, stem.beta)
         o = stem.w_codes.shape[0]
         stem_out = self._buf((B, h2, h2, o), torch.float32)
@@ -372,34 +386,93 @@ class W4A8ResNetEngine:
             step(s)
 
     def capture(self) -> None:
-        """Runs the chain once eagerly, then captures it as a CUDA graph."""
+        """Runs the chain once eagerly, then captures one CUDA graph per
+        input slot."""
+        graphs = []
         with torch.cuda.device(self.device):
+            self._slot = 0
             self.run_steps()
             torch.cuda.synchronize(self.device)
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                self.run_steps()
+            for slot in range(len(self.inputs)):
+                self._slot = slot
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self.run_steps()
+                graphs.append(g)
             torch.cuda.synchronize(self.device)
-        self.graph = g
+        self._slot = 0
+        self.graphs = graphs
+        self.graph = graphs[0]
 
-    def forward(self, images: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """images: float32 [batch, 3, H, W] on the engine's device (None:
-        the input buffer ``self.images`` was filled in place)."""
-        if images is not None and images.data_ptr() != self.images.data_ptr():
-            if images.shape != self.images.shape:
-                raise ValueError(f"expected images {tuple(self.images.shape)}, got {tuple(images.shape)}")
-            self.images.copy_(images, non_blocking=True)
+    def forward(self, images: Optional[torch.Tensor] = None, slot: int = 0) -> torch.Tensor:
+        """images: float32 [batch, 3, H, W] on the engine's device, copied
+        into input slot ``slot`` (None: the slot ``self.inputs[slot]`` was
+        filled in place). Runs on the current stream."""
+        buf = self.inputs[slot]
+        if images is not None and images.data_ptr() != buf.data_ptr():
+            if images.shape != buf.shape:
+                raise ValueError(f"expected images {tuple(buf.shape)}, got {tuple(images.shape)}")
+            buf.copy_(images, non_blocking=True)
         with torch.cuda.device(self.device):
             if self.use_graph:
                 if self.graph is None:
                     self.capture()
-                self.graph.replay()
+                self.graphs[slot].replay()
             else:
+                self._slot = slot
                 self.run_steps()
+                self._slot = 0
         return self.logits
+
+    def infer_host(self, batches, out: Optional[List[torch.Tensor]] = None,
+                   copy_stream: Optional[torch.cuda.Stream] = None,
+                   post: Optional[Callable[[torch.Tensor], None]] = None) -> List[torch.Tensor]:
+        """Serving loop over host batches (pinned float32 [batch, 3, H, W]):
+        batch i+1 is uploaded on ``copy_stream`` into the free input slot
+        while batch i runs; logits come back into ``out[i]`` (pinned host
+        tensors, allocated when absent). ``post(logits)``, when given, runs
+        on the compute stream after each forward (e.g. the data-parallel
+        logits gather). Returns ``out``; completion is ordered on the current
+        stream (synchronise before reading)."""
+        batches = list(batches)
+        if out is None:
+            out = [torch.empty(tuple(self.logits.shape), dtype=torch.float32).pin_memory() for _ in batches]
+        with torch.cuda.device(self.device):
+            if self.use_graph and self.graph is None:
+                self.capture()
+            compute = torch.cuda.current_stream(self.device)
+            copy_stream = copy_stream or torch.cuda.Stream(self.device)
+            copied = [torch.cuda.Event() for _ in self.inputs]
+            consumed = [torch.cuda.Event() for _ in self.inputs]
+            start = torch.cuda.Event()
+            start.record(compute)
+            copy_stream.wait_event(start)
+
+            def upload(i: int) -> None:
+                slot = i % len(self.inputs)
+                with torch.cuda.stream(copy_stream):
+                    if i >= len(self.inputs):
+                        copy_stream.wait_event(consumed[slot])
+                    self.inputs[slot].copy_(batches[i], non_blocking=True)
+                    copied[slot].record(copy_stream)
+
+            if batches:
+                upload(0)
+            for i in range(len(batches)):
+                slot = i % len(self.inputs)
+                if i + 1 < len(batches):
+                    upload(i + 1)
+                compute.wait_event(copied[slot])
+                self.forward(slot=slot)
+                consumed[slot].record(compute)
+                if post is not None:
+                    post(self.logits)
+                out[i].copy_(self.logits, non_blocking=True)
+        return out
 
     __call__ = forward
 
     def release(self) -> None:
-        """Drops the CUDA graph (before destroying process groups / exit)."""
+        """Drops the CUDA graphs (before destroying process groups / exit)."""
         self.graph = None
+        self.graphs = []

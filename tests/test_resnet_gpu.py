@@ -71,3 +71,16 @@ def test_converted_module_path_runs(cuda):
         got = model(images.to(cuda)).cpu().numpy()
     assert ro.top1_agreement(got, want) == 1.0
     assert ro.rel_err(got, want) < 5e-2
+
+
+def test_infer_host_pipeline_matches_oracle(cuda):
+    """Overlapped serving loop: three host batches through the two input
+    slots; every batch's logits equal the oracle's for that batch."""
+    model = build_lsq_resnet("resnet18", seed=7)
+    eng = W4A8ResNetEngine(model, 2, device=cuda, use_graph=True)
+    batches = [synthetic_images(2, seed=s).pin_memory() for s in (10, 11, 12)]
+    outs = eng.infer_host(batches)
+    torch.cuda.synchronize()
+    for i, (b, o) in enumerate(zip(batches, outs)):
+        _check(o, ro.resnet_forward(model, b.numpy()), f"infer_host batch {i}")
+    eng.release()
