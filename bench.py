@@ -181,6 +181,33 @@ def gemm_tops(device) -> dict:
     return {"shape_mnk": [m, n, k], "ms": round(ms, 4), "tops": round(tops, 1)}
 
 
+def fp16_cudnn_rate(device, batch: int, arch: str) -> dict:
+    """The same network in FP16 through torchvision + cuDNN (channels_last,
+    cudnn.benchmark, CUDA graph): the library path the W4A8 model must beat."""
+    import torchvision
+
+    torch.backends.cudnn.benchmark = True
+    net = getattr(torchvision.models, arch)(weights=None).to(device).half().eval()
+    net = net.to(memory_format=torch.channels_last)
+    x = torch.randn((batch, 3, 224, 224), device=device, dtype=torch.float16).to(memory_format=torch.channels_last)
+    with torch.no_grad():
+        for _ in range(3):
+            net(x)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device)
+        s.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(s):
+            net(x)
+        torch.cuda.current_stream(device).wait_stream(s)
+        with torch.cuda.graph(g):
+            net(x)
+        ms = time_events(g.replay, iters=30, warmup=3)
+    del g
+    return {"value": batch / (ms * 1e-3), "unit": "images/s", "ms_per_batch": round(ms, 4),
+            "config": f"torchvision {arch}, fp16, channels_last, cudnn.benchmark, CUDA graph, bs{batch}"}
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     import int4_int8_ext as ext
     from quant_pipeline.runtime.engine import W4A8ResNetEngine
@@ -306,6 +333,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             g.update(frac_of_int8_peak=round(g["tops"] / int8_peak, 4),
                      frac_of_nominal=round(g["tops"] / INT8_NOMINAL_TOPS, 4))
             line["gemm_int8"] = g
+            fp16 = fp16_cudnn_rate(device, B, args.arch)
+            fp16["w4a8_speedup"] = round(value / fp16["value"], 3)
+            line["fp16_cudnn"] = fp16
             torch.set_num_threads(os.cpu_count())
             line["cpu_baseline"] = cpu_oracle_rate(model, 24)
     engine.release()

@@ -37,7 +37,7 @@ int launch_t(const CUtensorMap& tA, const CUtensorMap& tW, const CUtensorMap* tH
       return W4A8_ERR_LAUNCH;
     if (dev >= 0 && dev < 64) attr_done[dev] = true;
   }
-  kern<<<grid, kThreads, kSmemAttr, st>>>(tA, tW, tH[0], tH[1], tH[2], tH[3], p);
+  kern<<<grid, Roles<CV>::kThreads, kSmemAttr, st>>>(tA, tW, tH[0], tH[1], tH[2], tH[3], p);
   return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH;
 }
 

@@ -6,12 +6,13 @@
 // Rows of A are GEMM rows (GEMM mode) or a 16x8 block of output pixels of
 // one image (conv mode); columns are output features / channels.
 //
-// Warp roles (512 threads):
+// Warp roles (Roles<conv>: 768 threads for the conv, 512 for the GEMM):
 //   warp 0       TMA producer (one elected lane)
 //   warp 1       TMEM owner + MMA issuer (one elected lane)
-//   warps 4-11   epilogue: tcgen05.ld -> fused LSQ epilogue -> global stores;
-//                warp w reads TMEM lanes 32*(w%4).. and column half (w-4)/4
-//   warps 12-15  int4 unpack: the packed nibbles land (TMA) in the upper half
+//   warps 4..    epilogue (16 or 8 warps): tcgen05.ld -> fused LSQ epilogue ->
+//                global stores; warp w reads TMEM lanes 32*(w%4).. and the
+//                column slice (w-4)/4 of the tile
+//   last 4 warps int4 unpack: the packed nibbles land (TMA) in the upper half
 //                of the int8 B stage and are expanded in place into the
 //                128B-swizzled int8 tile
 // The accumulator is double-buffered in TMEM so the epilogue of tile i
@@ -26,9 +27,14 @@ namespace w4a8 {
 
 constexpr int kBM = 128;          // rows per tile (MMA M)
 constexpr int kBK = 128;          // K bytes per k-block (one 128B swizzle atom)
-constexpr int kThreads = 512;
-constexpr int kEpiWarps = 8;      // warps 4..11
-constexpr int kUnpackWarp0 = 12;  // warps 12..15
+// Epilogue warps: the conv (short K, epilogue-heavy) uses 16, the GEMM
+// (long K, main-loop bound) 8; the 4 unpack warps follow them.
+template <bool kConv>
+struct Roles {
+  static constexpr int kEpiWarps = kConv ? 16 : 8;
+  static constexpr int kUnpackWarp0 = 4 + kEpiWarps;
+  static constexpr int kThreads = (kUnpackWarp0 + 4) * 32;
+};
 constexpr int kMaxStages = 8;
 constexpr int kMaxHaloStages = 6;
 constexpr int kMaxSteps = 64;     // conv MMA K-steps (32 B) per channel group
@@ -145,29 +151,7 @@ __device__ __forceinline__ void epilogue16(const EpiParams& e, const EpiConsts& 
     }
     return;
   }
-  float a[16], b[16], y[16];
-  if (ncols == 16 && e.alpha && (reinterpret_cast<uintptr_t>(e.alpha + n) & 15) == 0) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(e.alpha + n) + i);
-      a[4 * i] = v.x; a[4 * i + 1] = v.y; a[4 * i + 2] = v.z; a[4 * i + 3] = v.w;
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) a[i] = (e.alpha && i < ncols) ? __ldg(e.alpha + n + i) : e.alpha_scalar;
-  }
-  if (e.beta) {
-    if (ncols == 16 && (reinterpret_cast<uintptr_t>(e.beta + n) & 15) == 0) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(e.beta + n) + i);
-        b[4 * i] = v.x; b[4 * i + 1] = v.y; b[4 * i + 2] = v.z; b[4 * i + 3] = v.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) b[i] = i < ncols ? __ldg(e.beta + n + i) : 0.0f;
-    }
-  }
+  float y[16];
   // int32 -> float32: exact add-and-subtract of 1.5*2^23 unless a value
   // needs more than 22 bits (checked once for all 16).
   uint32_t oor = 0;
@@ -180,10 +164,33 @@ __device__ __forceinline__ void epilogue16(const EpiParams& e, const EpiConsts& 
 #pragma unroll
     for (int i = 0; i < 16; ++i) y[i] = __int2float_rn(int(acc[i]));
   }
+  // y = y * alpha (+ beta), four columns at a time.
+  const bool vec_ab = ncols == 16 && (!e.alpha || (reinterpret_cast<uintptr_t>(e.alpha + n) & 15) == 0) &&
+                      (!e.beta || (reinterpret_cast<uintptr_t>(e.beta + n) & 15) == 0);
+  if (vec_ab) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    y[i] = __fmul_rn(y[i], a[i]);
-    if (e.beta) y[i] = __fadd_rn(y[i], b[i]);
+    for (int g = 0; g < 4; ++g) {
+      float4 av = make_float4(e.alpha_scalar, e.alpha_scalar, e.alpha_scalar, e.alpha_scalar);
+      if (e.alpha) av = __ldg(reinterpret_cast<const float4*>(e.alpha + n) + g);
+      y[4 * g] = __fmul_rn(y[4 * g], av.x);
+      y[4 * g + 1] = __fmul_rn(y[4 * g + 1], av.y);
+      y[4 * g + 2] = __fmul_rn(y[4 * g + 2], av.z);
+      y[4 * g + 3] = __fmul_rn(y[4 * g + 3], av.w);
+      if (e.beta) {
+        const float4 bv = __ldg(reinterpret_cast<const float4*>(e.beta + n) + g);
+        y[4 * g] = __fadd_rn(y[4 * g], bv.x);
+        y[4 * g + 1] = __fadd_rn(y[4 * g + 1], bv.y);
+        y[4 * g + 2] = __fadd_rn(y[4 * g + 2], bv.z);
+        y[4 * g + 3] = __fadd_rn(y[4 * g + 3], bv.w);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float av = (e.alpha && i < ncols) ? __ldg(e.alpha + n + i) : e.alpha_scalar;
+      y[i] = __fmul_rn(y[i], av);
+      if (e.beta) y[i] = __fadd_rn(y[i], i < ncols ? __ldg(e.beta + n + i) : 0.0f);
+    }
   }
   if (e.residual) {
     const float* res = e.residual + prow * e.res_ld + n;
@@ -304,11 +311,14 @@ __device__ __forceinline__ bool row_coords(const KParams& p, int mt, int m, long
 
 // ------------------------------ kernel -------------------------------------
 template <int BN, bool kInt4, bool kConv>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
     w4a8_mma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                     const __grid_constant__ CUtensorMap tmH0, const __grid_constant__ CUtensorMap tmH1,
                     const __grid_constant__ CUtensorMap tmH2, const __grid_constant__ CUtensorMap tmH3,
                     const __grid_constant__ KParams p) {
+  constexpr int kEpiWarps = Roles<kConv>::kEpiWarps;
+  constexpr int kUnpackWarp0 = Roles<kConv>::kUnpackWarp0;
+  constexpr int kSlices = kEpiWarps / 4;  // column slices per TMEM lane quadrant
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_full[kMaxStages];
   __shared__ __align__(8) uint64_t bar_ready[kMaxStages];
@@ -517,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 4 && warp < 4 + kEpiWarps) {
     // ----------------------------- epilogue --------------------------------
     const int q = warp & 3;
-    const int half = (warp - 4) >> 2;
+    const int slice = (warp - 4) >> 2;
     const int m = q * 32 + lane;
     EpiConsts k;
     k.rs = p.epi.out_kind == 3 ? __frcp_rn(p.epi.out_scale) : 1.0f;
@@ -540,15 +550,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool valid = row_coords<kConv>(p, mt, m, out_off, prow);
       const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + buf * BN;
 #pragma unroll 1
-      for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
-        uint32_t acc[32];
-        tmem_ld16(t_addr + c0, *reinterpret_cast<uint32_t(*)[16]>(acc));
-        tmem_ld16(t_addr + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(acc + 16));
+      for (int c0 = slice * (BN / kSlices); c0 < (slice + 1) * (BN / kSlices); c0 += 16) {
+        uint32_t acc[16];
+        tmem_ld16(t_addr + c0, acc);
         tmem_ld_wait();
         if (valid) {
           const int n = nt * BN + c0;
           epilogue16(p.epi, k, acc, n, out_off + (long long)n * p.epi.s_ch, prow);
-          epilogue16(p.epi, k, acc + 16, n + 16, out_off + (long long)(n + 16) * p.epi.s_ch, prow);
         }
       }
       tc_fence_before();
