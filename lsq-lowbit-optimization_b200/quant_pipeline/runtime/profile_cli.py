@@ -37,22 +37,37 @@ def _time(fn, iters: int, warmup: int) -> float:
 
 
 def conv(a) -> dict:
+    """One conv launch. --ho overrides the output size (the space-to-depth
+    stem pads 2 top/left, 1 bottom/right); --out f32 writes float32 (stem);
+    --residual adds a float32 identity and a float32 side output (the last
+    conv of a residual block)."""
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(0)
-    ho = (a.h + 2 * a.pad - a.k) // a.stride + 1
+    ho = a.ho if a.ho else (a.h + 2 * a.pad - a.k) // a.stride + 1
     x = torch.randint(0, 128, (a.n, a.h, a.h, a.c), dtype=torch.int8, device=dev, generator=g)
     ktot = a.k * a.k * a.c
-    ldw = -(-(ktot // 2) // 16) * 16
-    w = torch.randint(0, 256, (a.o, ldw), dtype=torch.uint8, device=dev, generator=g)
+    wb = ktot // 2 if a.wbits == 4 else ktot
+    ldw = -(-wb // 16) * 16
+    w = torch.randint(0, 256 if a.wbits == 4 else 127, (a.o, ldw), dtype=torch.uint8, device=dev, generator=g)
     alpha = torch.rand(a.o, device=dev, generator=g) * 1e-3
     beta = torch.randn(a.o, device=dev, generator=g) * 1e-2
-    out = torch.empty((a.n, ho, ho, a.o), dtype=torch.int8, device=dev)
+    kind = ext.OUT_F32 if a.out == "f32" else ext.OUT_S8
+    out = torch.empty((a.n, ho, ho, a.o), dtype=torch.float32 if a.out == "f32" else torch.int8, device=dev)
+    res = aux = None
+    if a.residual:
+        res = torch.randn((a.n, ho, ho, a.o), device=dev, generator=g)
+        aux = torch.empty_like(res)
     geom = ext.ConvGeom(a.n, a.h, a.h, a.c, a.k, a.k, a.stride, a.pad, a.pad, ho, ho, a.o, ext.LAYOUT_NHWC, a.o)
-    epi = ext.make_epilogue(ext.OUT_S8, alpha=alpha, beta=beta, relu=True, out_scale=0.05, qn=0, qp=127)
-    ms = _time(lambda: ext.conv2d_nhwc(x, w, ext.W_INT4, geom, epi, out), a.iters, a.warmup)
+    epi = ext.make_epilogue(kind, alpha=alpha, beta=beta, relu=True, out_scale=0.05, qn=0, qp=127,
+                            residual=res, res_ld=a.o, aux=aux, aux_ld=a.o)
+    wkind = ext.W_INT4 if a.wbits == 4 else ext.W_INT8
+    ms = _time(lambda: ext.conv2d_nhwc(x, w, wkind, geom, epi, out), a.iters, a.warmup)
     ops = 2.0 * a.n * ho * ho * a.o * ktot
-    nbytes = x.numel() + out.numel() + a.o * ktot / 2
-    return {"op": "conv", "shape": vars(a), "ms": ms, "tops": ops / ms / 1e9, "gbs": nbytes / ms / 1e6}
+    nbytes = x.numel() + out.numel() * out.element_size() + a.o * wb
+    if a.residual:
+        nbytes += 2 * res.numel() * 4
+    return {"op": "conv", "shape": vars(a), "ms": ms, "tops": ops / ms / 1e9, "gbs": nbytes / ms / 1e6,
+            "alg_ops": ops, "alg_bytes": nbytes}
 
 
 def gemm(a) -> dict:
@@ -84,8 +99,10 @@ def main() -> None:
     p = argparse.ArgumentParser()
     sub = p.add_subparsers(dest="cmd", required=True)
     c = sub.add_parser("conv")
-    for k, v in dict(n=256, h=56, c=64, o=64, k=3, stride=1, pad=1).items():
+    for k, v in dict(n=256, h=56, c=64, o=64, k=3, stride=1, pad=1, ho=0, wbits=4).items():
         c.add_argument(f"--{k}", type=int, default=v)
+    c.add_argument("--out", choices=["s8", "f32"], default="s8")
+    c.add_argument("--residual", action="store_true")
     gm = sub.add_parser("gemm")
     for k, v in dict(m=4096, n=8192, k=8192).items():
         gm.add_argument(f"--{k}", type=int, default=v)
