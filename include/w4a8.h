@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define W4A8_ABI_VERSION 1
+#define W4A8_ABI_VERSION 2
 
 /* Status codes: 0 ok, > 0 argument errors (nothing was launched),
  * < 0 runtime errors. */
@@ -116,12 +116,20 @@ typedef struct {
   int o;             /* output channels */
   int out_layout;    /* W4A8_LAYOUT_NHWC or W4A8_LAYOUT_NCHW */
   int64_t ldo;       /* NHWC: output elements per pixel (>= o) */
+  int pool;          /* 1: fuse a 3x3/s2/p1 max pool after the epilogue
+                        (o <= 64, NHWC out); outputs are then pooled, of size
+                        ((ho-1)/2+1, (wo-1)/2+1). 0: no pooling. */
 } w4a8_conv_geom;
 
 /*
  * Implicit-GEMM convolution: out = epilogue(conv(x, W)); rows of the GEMM
  * are output pixels (n, oh, ow), columns output channels. residual / aux of
  * the epilogue are NHWC fp32 with res_ld / aux_ld elements per pixel.
+ * With geom->pool the 3x3/s2/p1 max pool is taken over the int32
+ * accumulators before the epilogue (exact: the epilogue is monotone in the
+ * accumulator, increasing where alpha >= 0 and decreasing where alpha < 0,
+ * so the extreme accumulator of each window yields the pooled value);
+ * residual is not allowed then.
  * Replaces the lowering + GEMM + postprocess chain of
  * conv3x3_int4_int8_s1_p1 and conv1x1_int4_int8
  * (csrc/int4_int8_kernels.cu:323-373, 429-500).

@@ -6,7 +6,7 @@
 
 #include <cstdint>
 
-#include "../../include/w4a8.h"
+#include "w4a8.h"
 
 namespace {
 

@@ -197,6 +197,10 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   if (g->c != 16 && (g->c % 32 || (g->c > 128 && g->c % 128))) return W4A8_ERR_UNSUPPORTED;
   if (g->out_layout != W4A8_LAYOUT_NHWC && g->out_layout != W4A8_LAYOUT_NCHW) return W4A8_ERR_ARG;
   if (g->out_layout == W4A8_LAYOUT_NHWC && g->ldo < g->o) return W4A8_ERR_ARG;
+  if (g->pool != 0 && g->pool != 1) return W4A8_ERR_ARG;
+  if (g->pool && (g->o > 64 || g->out_layout != W4A8_LAYOUT_NHWC || epi->residual ||
+                  (epi->out_kind != W4A8_OUT_S8 && epi->out_kind != W4A8_OUT_F32) || (g->o % 4)))
+    return W4A8_ERR_UNSUPPORTED;
   if (g->n == 0) return W4A8_OK;
   if (!x || !W || !out) return W4A8_ERR_ARG;
   const int s = g->stride;
@@ -240,8 +244,16 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   ConvParams& cp = p.conv;
   cp.ho = g->ho;
   cp.wo = g->wo;
-  cp.tiles_h = (g->ho + kTileH - 1) / kTileH;
-  cp.tiles_w = (g->wo + kTileW - 1) / kTileW;
+  cp.pool = g->pool;
+  if (g->pool) {
+    cp.pho = (g->ho - 1) / 2 + 1;
+    cp.pwo = (g->wo - 1) / 2 + 1;
+    cp.tiles_h = (cp.pho + kPoolRows - 1) / kPoolRows;
+    cp.tiles_w = (cp.pwo + kPoolCols - 1) / kPoolCols;
+  } else {
+    cp.tiles_h = (g->ho + kTileH - 1) / kTileH;
+    cp.tiles_w = (g->wo + kTileW - 1) / kTileW;
+  }
   cp.planes = planes;
   cp.halo_w = kTileW + span_w;
   cp.halo_h = kTileH + span_h;
@@ -305,11 +317,14 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   // at least two halo stages, the CTA loads and unpacks the weights once and
   // then streams only input halos.
   const uint32_t bres_bytes = uint32_t(p.num_kb) * per_stage;
+  // The fused pool stages one tile of int32 accumulators (128 x 68 words).
+  const uint32_t pool_bytes = g->pool ? uint32_t(kBM * kPoolPitch * 4 + 1023) & ~1023u : 0u;
+  const int budget = kSmemBudget - int(pool_bytes);
   p.b_resident = 0;
-  if (p.tiles_n == 1 && bres_bytes + 2 * cp.halo_bytes <= uint32_t(kSmemBudget)) {
+  if (p.tiles_n == 1 && bres_bytes + 2 * cp.halo_bytes <= uint32_t(budget)) {
     p.b_resident = 1;
     p.stages = 1;
-    p.halo_stages = std::min<int>(kMaxHaloStages, (kSmemBudget - bres_bytes) / cp.halo_bytes);
+    p.halo_stages = std::min<int>(kMaxHaloStages, (budget - bres_bytes) / cp.halo_bytes);
     p.bres_tx_bytes = i4 ? bres_bytes / 2 : bres_bytes;
   } else {
     // Deepest halo pipeline (each stage is one tile's input window) that
@@ -317,13 +332,14 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
     p.stages = 0;
     for (int hs = kMaxHaloStages; hs >= 1 && p.stages < 3; --hs) {
       p.halo_stages = hs;
-      p.stages = pick_stages(per_stage, hs * cp.halo_bytes);
+      p.stages = pick_stages(per_stage, hs * cp.halo_bytes + pool_bytes);
     }
     if (p.stages < 2) return W4A8_ERR_UNSUPPORTED;
   }
   p.a_off = 0;
   p.h_off = 0;
-  p.b_off = p.halo_stages * cp.halo_bytes;
+  cp.pool_off = p.halo_stages * cp.halo_bytes;
+  p.b_off = cp.pool_off + pool_bytes;
   p.bp_off = 0;
   p.tx_bytes = i4 ? p.b_stage_bytes / 2 : p.b_stage_bytes;
   p.tmem_cols = 2 * bn;

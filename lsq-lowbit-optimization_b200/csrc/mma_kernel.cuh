@@ -12,7 +12,7 @@
 //   warps 4..    epilogue (16 or 8 warps): tcgen05.ld -> fused LSQ epilogue ->
 //                global stores; warp w reads TMEM lanes 32*(w%4).. and the
 //                column slice (w-4)/4 of the tile
-//   last 4 warps int4 unpack: the packed nibbles land (TMA) in the upper half
+//   last warps  int4 unpack (4 conv / 8 GEMM): the packed nibbles land (TMA) in the upper half
 //                of the int8 B stage and are expanded in place into the
 //                128B-swizzled int8 tile
 // The accumulator is double-buffered in TMEM so the epilogue of tile i
@@ -21,6 +21,8 @@
 
 #include <cuda_fp16.h>
 
+#include <climits>
+
 #include "ptx.cuh"
 
 namespace w4a8 {
@@ -28,18 +30,23 @@ namespace w4a8 {
 constexpr int kBM = 128;          // rows per tile (MMA M)
 constexpr int kBK = 128;          // K bytes per k-block (one 128B swizzle atom)
 // Epilogue warps: the conv (short K, epilogue-heavy) uses 16, the GEMM
-// (long K, main-loop bound) 8; the 4 unpack warps follow them.
+// (long K, main-loop bound) 8. The unpack warps follow them: 4 for the
+// conv, 8 for the GEMM, whose weight expansion runs every k-block.
 template <bool kConv>
 struct Roles {
   static constexpr int kEpiWarps = kConv ? 16 : 8;
+  static constexpr int kUnpackWarps = kConv ? 4 : 8;
   static constexpr int kUnpackWarp0 = 4 + kEpiWarps;
-  static constexpr int kThreads = (kUnpackWarp0 + 4) * 32;
+  static constexpr int kThreads = (kUnpackWarp0 + kUnpackWarps) * 32;
 };
 constexpr int kMaxStages = 8;
 constexpr int kMaxHaloStages = 6;
 constexpr int kMaxSteps = 64;     // conv MMA K-steps (32 B) per channel group
 constexpr int kTileH = 16;        // conv: output rows per tile (one 8-row core group each)
 constexpr int kTileW = 8;         // conv: output columns per tile
+// Fused max pool: a 16x8 conv tile at origin (14*th - 1, 6*tw - 1) holds
+// every 3x3/s2 window of a 7x3 block of pooled outputs.
+constexpr int kPoolRows = 7, kPoolCols = 3, kPoolPitch = 68;  // staging row pitch (int32)
 
 struct EpiParams {
   void* out;
@@ -70,6 +77,9 @@ struct ConvParams {
   uint32_t halo_tx_bytes;  // bytes the TMA loads of one stage deliver
   int slot_qh[4], slot_qw[4];  // per slot: TMA start offset in phase-view units
   int kb_per_group;
+  int pool;                // 1: fused 3x3/s2/p1 max pool (tiles overlap by one row/column)
+  int pho, pwo;            // pooled output size
+  uint32_t pool_off;       // smem offset of the int32 accumulator staging tile
   uint32_t step_off[kMaxSteps];  // smem byte offset of the first 16 B K-chunk
   uint32_t step_lbo[kMaxSteps];  // byte distance to the second 16 B K-chunk
 };
@@ -309,6 +319,87 @@ __device__ __forceinline__ bool row_coords(const KParams& p, int mt, int m, long
   }
 }
 
+// Fused 3x3/s2/p1 max pool of one conv tile (BN <= 64 channels): every
+// epilogue warp stages its int32 accumulators in smem and frees the TMEM
+// buffer; after a named barrier each thread reduces one (pooled pixel,
+// 4 channels) window over in-image conv pixels, keeping the max and the
+// min (the epilogue is increasing in acc where alpha >= 0, decreasing where
+// alpha < 0), applies the epilogue to the selected accumulator and stores
+// the pooled codes (out) and float32 values (aux).
+template <int BN, int kEpiWarps>
+__device__ __forceinline__ void pool_epilogue(const KParams& p, const EpiConsts& k, uint32_t t_addr,
+                                              uint8_t* stage_bytes, int mt, int m, int slice, int slices, int ew,
+                                              int lane, uint64_t* tempty) {
+  int32_t* stg = reinterpret_cast<int32_t*>(stage_bytes);
+  for (int c0 = slice * (BN / slices); c0 < (slice + 1) * (BN / slices); c0 += 16) {
+    uint32_t acc[16];
+    tmem_ld16(t_addr + c0, acc);
+    tmem_ld_wait();
+    int4* dst = reinterpret_cast<int4*>(stg + m * kPoolPitch + c0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      dst[i] = make_int4(int(acc[4 * i]), int(acc[4 * i + 1]), int(acc[4 * i + 2]), int(acc[4 * i + 3]));
+  }
+  tc_fence_before();
+  mbar_arrive(tempty);
+  bar_sync(2, kEpiWarps * 32);
+  const ConvParams& c = p.conv;
+  const EpiParams& e = p.epi;
+  const int per_img = c.tiles_h * c.tiles_w;
+  const int img = mt / per_img;
+  const int rem = mt - img * per_img;
+  const int th = rem / c.tiles_w;
+  const int tw = rem - th * c.tiles_w;
+  const int oh0 = th * 2 * kPoolRows - 1, ow0 = tw * 2 * kPoolCols - 1;
+  constexpr int kQuads = BN / 4;
+  const int w = ew * 32 + lane;
+  if (w < kPoolRows * kPoolCols * kQuads) {
+    const int pix = w / kQuads, quad = w - pix * kQuads;
+    const int pr_l = pix / kPoolCols, pc_l = pix - pr_l * kPoolCols;
+    const int pr = th * kPoolRows + pr_l, pc = tw * kPoolCols + pc_l;
+    const int ch = quad * 4;
+    if (pr < c.pho && pc < c.pwo && ch < e.n_total) {
+      int mx[4] = {INT_MIN, INT_MIN, INT_MIN, INT_MIN}, mn[4] = {INT_MAX, INT_MAX, INT_MAX, INT_MAX};
+#pragma unroll
+      for (int dy = 0; dy < 3; ++dy) {
+        const int lr = 2 * pr_l + dy, r = oh0 + lr;
+        if (r < 0 || r >= c.ho) continue;
+#pragma unroll
+        for (int dx = 0; dx < 3; ++dx) {
+          const int lc = 2 * pc_l + dx, col = ow0 + lc;
+          if (col < 0 || col >= c.wo) continue;
+          const int4 v = *reinterpret_cast<const int4*>(stg + (lr * kTileW + lc) * kPoolPitch + ch);
+          mx[0] = max(mx[0], v.x); mx[1] = max(mx[1], v.y); mx[2] = max(mx[2], v.z); mx[3] = max(mx[3], v.w);
+          mn[0] = min(mn[0], v.x); mn[1] = min(mn[1], v.y); mn[2] = min(mn[2], v.z); mn[3] = min(mn[3], v.w);
+        }
+      }
+      float y[4];
+      int q[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float a = e.alpha ? __ldg(e.alpha + ch + i) : e.alpha_scalar;
+        float v = __fmul_rn(__int2float_rn(a >= 0.0f ? mx[i] : mn[i]), a);
+        if (e.beta) v = __fadd_rn(v, __ldg(e.beta + ch + i));
+        if (e.relu) v = fmaxf(v, 0.0f);
+        y[i] = v;
+        q[i] = int(__float_as_int(__fadd_rn(fminf(fmaxf(lsq_guard(v, __fmul_rn(v, k.rs), e.out_scale), k.qnf),
+                                                    k.qpf), 12582912.0f)) - 0x4B400000);
+      }
+      const long long prow = ((long long)img * c.pho + pr) * c.pwo + pc;
+      if (e.aux) *reinterpret_cast<float4*>(e.aux + prow * e.aux_ld + ch) = make_float4(y[0], y[1], y[2], y[3]);
+      if (e.out_kind == 3) {
+        const uint32_t word = (uint32_t(q[0]) & 0xFFu) | ((uint32_t(q[1]) & 0xFFu) << 8) |
+                              ((uint32_t(q[2]) & 0xFFu) << 16) | ((uint32_t(q[3]) & 0xFFu) << 24);
+        *reinterpret_cast<uint32_t*>(static_cast<int8_t*>(e.out) + prow * e.s_pix + ch) = word;
+      } else if (e.out_kind == 1) {
+        *reinterpret_cast<float4*>(static_cast<float*>(e.out) + prow * e.s_pix + ch) =
+            make_float4(y[0], y[1], y[2], y[3]);
+      }
+    }
+  }
+  bar_sync(2, kEpiWarps * 32);  // the staging tile is free for the next tile
+}
+
 // ------------------------------ kernel -------------------------------------
 template <int BN, bool kInt4, bool kConv>
 __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
@@ -318,6 +409,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
                     const __grid_constant__ KParams p) {
   constexpr int kEpiWarps = Roles<kConv>::kEpiWarps;
   constexpr int kUnpackWarp0 = Roles<kConv>::kUnpackWarp0;
+  constexpr int kUnpackThreads = Roles<kConv>::kUnpackWarps * 32;
   constexpr int kSlices = kEpiWarps / 4;  // column slices per TMEM lane quadrant
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_full[kMaxStages];
@@ -341,7 +433,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&bar_full[s], 1);
-      mbar_init(&bar_ready[s], 128);
+      mbar_init(&bar_ready[s], Roles<kConv>::kUnpackWarps);
       mbar_init(&bar_empty[s], 1);
     }
     for (int s = 0; s < p.halo_stages; ++s) {
@@ -354,7 +446,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
     }
     mbar_init(&bar_drain, 1);
     mbar_init(&bar_bres, 1);
-    mbar_init(&bar_bready, 128);
+    mbar_init(&bar_bready, Roles<kConv>::kUnpackWarps);
     abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -405,8 +497,9 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
           img = mt / per_img;
           const int rem = mt - img * per_img;
           const int th = rem / p.conv.tiles_w;
-          oh0 = th * kTileH;
-          ow0 = (rem - th * p.conv.tiles_w) * kTileW;
+          const int tw = rem - th * p.conv.tiles_w;
+          oh0 = p.conv.pool ? th * 2 * kPoolRows - 1 : th * kTileH;
+          ow0 = p.conv.pool ? tw * 2 * kPoolCols - 1 : tw * kTileW;
         }
         int g = 0, kb_in_g = 0;
         for (int kb = 0; ok && kb < p.num_kb; ++kb) {
@@ -546,6 +639,11 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       tc_fence_after();
       const int mt = t / p.tiles_n;
       const int nt = t - mt * p.tiles_n;
+      if (kConv && p.conv.pool) {
+        pool_epilogue<BN, kEpiWarps>(p, k, tmem_base + (uint32_t(q * 32) << 16) + buf * BN, base + p.conv.pool_off,
+                                     mt, m, slice, kSlices, warp - 4, lane, &bar_tempty[buf]);
+        continue;
+      }
       long long out_off = 0, prow = 0;
       const bool valid = row_coords<kConv>(p, mt, m, out_off, prow);
       const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + buf * BN;
@@ -567,48 +665,62 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
     // Phase 1 reads every packed chunk this thread owns into registers,
     // a named barrier orders all reads before any write, phase 2 writes the
     // int8 rows over the stage (the packed half is overwritten in place).
-    constexpr int kPer = BN * 8 / 128;
+    constexpr int kPer = BN * 8 / kUnpackThreads;
     const int ut = threadIdx.x - kUnpackWarp0 * 32;
+    // This thread's chunks (row r, 16-byte chunk c of the int8 row) are the
+    // same in every k-block: precompute packed-source and swizzled-target offsets.
+    uint32_t src_off[kPer], dst_off[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int idx = ut + kUnpackThreads * j;
+      const int r = idx >> 3, c = idx & 7;
+      src_off[j] = BN * (kBK / 2) + r * 64 + c * 8;
+      dst_off[j] = r * 128 + ((c ^ (r & 7)) << 4);
+    }
     int s = 0;
     uint32_t ph = 0;
     bool ok = true;
     const bool resident = kConv && p.b_resident;
-    if (resident) ok = bar_and(1, 128, mbar_wait(&bar_bres, 0, &abort_flag));
+    // One lane per warp polls the mbarrier (all 32 polling one word
+    // serialises on the shared-memory bank); __syncwarp then orders the
+    // rest of the warp after the observed phase.
+    auto wait_warp = [&](uint64_t* bar, uint32_t parity) -> bool {
+      int got = 1;
+      if (lane == 0) got = mbar_wait(bar, parity, &abort_flag) ? 1 : 0;
+      got = __shfl_sync(0xffffffffu, got, 0);
+      return got != 0;
+    };
+    if (resident) ok = bar_and(1, kUnpackThreads, wait_warp(&bar_bres, 0));
     const int passes = resident ? 1 : total_tiles;  // resident weights: one pass over the k-blocks
     for (int t = resident ? 0 : int(blockIdx.x); ok && t < passes; t += resident ? 1 : int(gridDim.x)) {
       for (int kb = 0; kb < p.num_kb; ++kb) {
         if (!resident) {
-          const bool got = mbar_wait(&bar_full[s], ph, &abort_flag);
-          if (!bar_and(1, 128, got)) { ok = false; break; }
+          if (!bar_and(1, kUnpackThreads, wait_warp(&bar_full[s], ph))) { ok = false; break; }
         }
         uint8_t* stage = base + p.b_off + (resident ? kb : s) * p.b_stage_bytes;
-        const uint8_t* src = stage + BN * (kBK / 2);
         uint2 v[kPer];
 #pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-          const int idx = ut + 128 * j;
-          v[j] = *reinterpret_cast<const uint2*>(src + (idx >> 3) * 64 + (idx & 7) * 8);
-        }
-        bar_sync(1, 128);
+        for (int j = 0; j < kPer; ++j) v[j] = *reinterpret_cast<const uint2*>(stage + src_off[j]);
+        bar_sync(1, kUnpackThreads);
 #pragma unroll
         for (int j = 0; j < kPer; ++j) {
-          const int idx = ut + 128 * j;
-          const int r = idx >> 3, c = idx & 7;
           uint4 o;
           unpack_nibbles8(v[j].x, o.x, o.y);
           unpack_nibbles8(v[j].y, o.z, o.w);
-          *reinterpret_cast<uint4*>(stage + r * 128 + ((c ^ (r & 7)) << 4)) = o;
+          *reinterpret_cast<uint4*>(stage + dst_off[j]) = o;
         }
         fence_proxy_async_smem();
         if (resident) {
-          bar_sync(1, 128);  // the next k-block's reads follow this one's writes
+          bar_sync(1, kUnpackThreads);
           continue;
         }
-        mbar_arrive(&bar_ready[s]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_ready[s]);
         if (++s == p.stages) { s = 0; ph ^= 1; }
       }
     }
-    if (resident && ok) mbar_arrive(&bar_bready);
+    __syncwarp();
+    if (resident && ok && lane == 0) mbar_arrive(&bar_bready);
     if (!ok && ut == 0) atomicOr(p.err, kErrTimeoutUnpack);
   }
 

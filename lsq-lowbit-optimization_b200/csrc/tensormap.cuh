@@ -9,7 +9,7 @@
 #include <cstdint>
 #include <cstring>
 
-#include "../../include/w4a8.h"
+#include "w4a8.h"
 
 namespace w4a8 {
 

@@ -70,6 +70,7 @@ class ConvGeom(ctypes.Structure):
         ("o", ctypes.c_int),
         ("out_layout", ctypes.c_int),
         ("ldo", ctypes.c_int64),
+        ("pool", ctypes.c_int),
     ]
 
 
@@ -88,7 +89,7 @@ _SIGNATURES = {
     "w4a8_abi_version": [],
     "w4a8_num_sms": [],
 }
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _lib_handle: Optional[ctypes.CDLL] = None
 

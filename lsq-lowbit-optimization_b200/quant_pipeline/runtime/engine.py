@@ -5,7 +5,8 @@ after ``convert_lsq_modules(model, convert_conv=True)`` swapped its INT4
 layers for ``Int4WeightInt8ActConv2d`` — into a fixed chain of libw4a8 calls:
 
   images f32 NCHW --s2d+quantise--> int8 [B,112,112,16]
-    --4x4 conv (the 7x7/s2 stem re-indexed, W8)--> f32 --maxpool--> f32 + codes
+    --4x4 conv (the 7x7/s2 stem re-indexed, W8) + BN + ReLU + 3x3/s2 max pool,
+      one launch--> pooled f32 + codes
     --per block: conv1 -> codes, [downsample -> f32 identity],
                  conv2/conv3 (+identity, ReLU) -> codes (+ f32 when needed)
     --avgpool+quantise--> int8 [B, C] --W8 GEMM--> logits f32 [B, classes]
@@ -187,9 +188,10 @@ class W4A8ResNetEngine:
                   relu: bool, qout: QParams = (1.0, -128, 127), residual: Optional[torch.Tensor] = None,
                   aux: Optional[torch.Tensor] = None, what: str = "conv",
                   macs_per_pixel: Optional[int] = None,
-                  out_hw: Optional[Tuple[int, int]] = None) -> Tuple[int, int, int, int]:
+                  out_hw: Optional[Tuple[int, int]] = None, pool: bool = False) -> Tuple[int, int, int, int]:
         """``out_hw`` overrides the symmetric-padding output size (the
-        space-to-depth stem pads 2 top/left and 1 bottom/right)."""
+        space-to-depth stem pads 2 top/left and 1 bottom/right); ``pool``
+        fuses the 3x3/s2/p1 max pool, so ``out``/``aux`` are pooled."""
         n, h, w, c = in_shape
         o, kh, kw, _ = spec.w_codes.shape
         if out_hw is None:
@@ -197,15 +199,16 @@ class W4A8ResNetEngine:
             wo = (w + 2 * spec.pad - kw) // spec.stride + 1
         else:
             ho, wo = out_hw
+        oh_, ow_ = ((ho - 1) // 2 + 1, (wo - 1) // 2 + 1) if pool else (ho, wo)
         for name, t in (("out", out), ("residual", residual), ("aux", aux)):
-            if t is not None and tuple(t.shape) != (n, ho, wo, o):
-                raise ValueError(f"{what}: {name} buffer {tuple(t.shape)} != output {(n, ho, wo, o)}")
+            if t is not None and tuple(t.shape) != (n, oh_, ow_, o):
+                raise ValueError(f"{what}: {name} buffer {tuple(t.shape)} != output {(n, oh_, ow_, o)}")
         if tuple(x.shape) != (n, h, w, c):
             raise ValueError(f"{what}: input buffer {tuple(x.shape)} != {(n, h, w, c)}")
-        pix = n * ho * wo
+        pix, opix = n * ho * wo, n * oh_ * ow_
         ops = 2.0 * pix * (macs_per_pixel if macs_per_pixel is not None else o * kh * kw * c)
-        nbytes = n * h * w * c + pix * o * out.element_size() + o * kh * kw * c * spec.w_bits / 8
-        nbytes += (pix * o * 4 if residual is not None else 0) + (pix * o * 4 if aux is not None else 0)
+        nbytes = n * h * w * c + opix * o * out.element_size() + o * kh * kw * c * spec.w_bits / 8
+        nbytes += (opix * o * 4 if residual is not None else 0) + (opix * o * 4 if aux is not None else 0)
         wk = _kernel_weights(spec.w_codes, spec.w_bits, c, self.device)
         alpha = spec.alpha.to(self.device)
         beta = spec.beta.to(self.device)
@@ -217,7 +220,8 @@ class W4A8ResNetEngine:
             self._add(self.lib.w4a8_gemm, (x.data_ptr(), c, wk.data_ptr(), wk.stride(0), kind, n * h * w, o, c,
                                            ctypes.byref(epi), out.data_ptr(), o), what, ops, nbytes)
         else:
-            geom = ext.ConvGeom(n, h, w, c, kh, kw, spec.stride, spec.pad, spec.pad, ho, wo, o, ext.LAYOUT_NHWC, o)
+            geom = ext.ConvGeom(n, h, w, c, kh, kw, spec.stride, spec.pad, spec.pad, ho, wo, o, ext.LAYOUT_NHWC, o,
+                                int(pool))
             self._keep.append(geom)
             self._add(self.lib.w4a8_conv2d, (x.data_ptr(), wk.data_ptr(), kind, wk.stride(0), ctypes.byref(geom),
                                              ctypes.byref(epi), out.data_ptr()), what, ops, nbytes)
@@ -246,7 +250,7 @@ class W4A8ResNetEngine:
                 params.append(b["ds"].qin)
             return params, (b["ds"] is None) or len(params) > 1
 
-        # Stem: s2d + quantise -> 4x4 conv (W8) -> f32 -> maxpool -> f32 + codes.
+        # Stem: s2d + quantise, then the fused conv + pool below.
         s_a, qn, qp = stem.qin
         # Two input slots: a graph is captured per slot so the next batch can
         # be uploaded into one slot while the other is being consumed.
@@ -268,21 +272,17 @@ class W4A8ResNetEngine:
         self.launches += 1
         stem4 = ConvSpec(stem_s2d_weights(stem.w_codes), stem.w_bits, 1, 2, stem.qin, stem.alpha, stem.beta)
         o = stem.w_codes.shape[0]
-        stem_out = self._buf((B, h2, h2, o), torch.float32)
         kh0, kw0, c0 = stem.w_codes.shape[1:]
-        self._add_conv(stem4, s2d, (B, h2, h2, 16), ext.OUT_F32, stem_out, relu=True, what="stem",
-                       macs_per_pixel=stem.w_codes.shape[0] * kh0 * kw0 * c0, out_hw=(h2, h2))
         hp = (h2 - 1) // 2 + 1
         params, need_f32 = consumers_of(0)
         act = Activation((B, hp, hp, o))
-        act.f32 = self._buf(act.shape, torch.float32) if need_f32 else None
         act.codes[params[0]] = self._buf(act.shape, torch.int8)
-        pool_f = act.f32 if act.f32 is not None else self._buf(act.shape, torch.float32)
-        if act.f32 is None:
-            act.f32 = pool_f
-        self._add(self.lib.w4a8_maxpool3x3s2, (stem_out.data_ptr(), pool_f.data_ptr(),
-                                               act.codes[params[0]].data_ptr(), B, h2, h2, o, hp, hp,
-                                               params[0][0], params[0][1], params[0][2]), "maxpool")
+        act.f32 = self._buf(act.shape, torch.float32) if (need_f32 or len(params) > 1) else None
+        # Stem conv + BN + ReLU + 3x3/s2 max pool in one launch: pooled codes
+        # for the first block and the pooled float32 identity.
+        self._add_conv(stem4, s2d, (B, h2, h2, 16), ext.OUT_S8, act.codes[params[0]], relu=True, qout=params[0],
+                       aux=act.f32, what="stem+maxpool", macs_per_pixel=o * kh0 * kw0 * c0, out_hw=(h2, h2),
+                       pool=True)
         for q in params[1:]:
             act.codes[q] = self._buf(act.shape, torch.int8)
             self._add_requant(act.f32, act.codes[q], q)

@@ -74,10 +74,14 @@ def gemm(a) -> dict:
     dev = torch.device("cuda")
     g = torch.Generator(device=dev).manual_seed(0)
     x = torch.randint(-128, 128, (a.m, a.k), dtype=torch.int8, device=dev, generator=g)
-    w = torch.randint(0, 256, (a.n, a.k // 2), dtype=torch.uint8, device=dev, generator=g)
+    if a.wbits == 4:
+        w = torch.randint(0, 256, (a.n, a.k // 2), dtype=torch.uint8, device=dev, generator=g)
+    else:
+        w = torch.randint(-128, 128, (a.n, a.k), dtype=torch.int8, device=dev, generator=g)
     out = torch.empty((a.m, a.n), dtype=torch.int32, device=dev)
     epi = ext.make_epilogue(ext.OUT_S32)
-    ms = _time(lambda: ext.gemm(x, w, ext.W_INT4, a.k, epi, out), a.iters, a.warmup)
+    wkind = ext.W_INT4 if a.wbits == 4 else ext.W_INT8
+    ms = _time(lambda: ext.gemm(x, w, wkind, a.k, epi, out), a.iters, a.warmup)
     ops = 2.0 * a.m * a.n * a.k
     nbytes = x.numel() + w.numel() + out.numel() * 4
     return {"op": "gemm", "shape": vars(a), "ms": ms, "tops": ops / ms / 1e9, "gbs": nbytes / ms / 1e6}
@@ -104,7 +108,7 @@ def main() -> None:
     c.add_argument("--out", choices=["s8", "f32"], default="s8")
     c.add_argument("--residual", action="store_true")
     gm = sub.add_parser("gemm")
-    for k, v in dict(m=4096, n=8192, k=8192).items():
+    for k, v in dict(m=4096, n=8192, k=8192, wbits=4).items():
         gm.add_argument(f"--{k}", type=int, default=v)
     r = sub.add_parser("resnet")
     r.add_argument("--batch", type=int, default=256)

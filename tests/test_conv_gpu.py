@@ -179,3 +179,44 @@ def test_lower_quantize_3x3_matches_oracle(cuda):
     assert_equal(got, orc.lower_quantize_3x3(x, 0.05, -128, 127, 50), "lowering")
     got = ext.lower_quantize_3x3_s1_p1(to_dev(x, cuda), 0.05, 2, 127, 46)
     assert_equal(got, orc.lower_quantize_3x3(x, 0.05, 2, 127, 46), "lowering qn>0")
+
+
+def test_conv_fused_maxpool(cuda):
+    """Stem-style conv with the 3x3/s2/p1 max pool fused into the epilogue;
+    alpha has both signs (pooling picks the max or min accumulator)."""
+    g = rng(21)
+    n, h, w, c, o = 2, 30, 26, 16, 64
+    xq = rand_i8(g, (n, h, w, c))
+    wt = rand_i8(g, (o, 4, 4, c))
+    alpha = g.uniform(1e-4, 1e-3, o).astype(np.float32)
+    alpha[::3] *= -1
+    beta = g.normal(0, 0.5, o).astype(np.float32)
+    acc = orc.conv_nhwc_s32(xq, wt, 1, 2, 2, h, w)
+    y = orc.epilogue(acc, alpha, beta, relu=True)
+    pooled = orc.maxpool3x3s2(y)
+    ph, pw = pooled.shape[1:3]
+    codes = torch.empty((n, ph, pw, o), dtype=torch.int8, device=cuda)
+    aux = torch.empty((n, ph, pw, o), dtype=torch.float32, device=cuda)
+    wk = to_dev(np.ascontiguousarray(wt.reshape(o, -1)), cuda)
+    geom = ext.ConvGeom(n, h, w, c, 4, 4, 1, 2, 2, h, w, o, ext.LAYOUT_NHWC, o, 1)
+    alpha_t, beta_t = to_dev(alpha, cuda), to_dev(beta, cuda)
+    epi = ext.make_epilogue(ext.OUT_S8, alpha=alpha_t, beta=beta_t, relu=True, out_scale=0.05, qn=0, qp=127,
+                            aux=aux, aux_ld=o)
+    ext.conv2d_nhwc(to_dev(xq, cuda), wk, ext.W_INT8, geom, epi, codes)
+    assert_equal(aux, pooled, "pooled f32")
+    assert_equal(codes, orc.quantize(pooled, 0.05, 0, 127), "pooled codes")
+
+
+def test_maxpool_kernel(cuda):
+    g = rng(22)
+    x = g.normal(0, 1, (2, 17, 12, 8)).astype(np.float32)
+    want = orc.maxpool3x3s2(x)
+    yf = torch.empty(want.shape, dtype=torch.float32, device=cuda)
+    yq = torch.empty(want.shape, dtype=torch.int8, device=cuda)
+    xd = to_dev(x, cuda)
+    with torch.cuda.device(cuda):
+        rc = ext.lib().w4a8_maxpool3x3s2(xd.data_ptr(), yf.data_ptr(), yq.data_ptr(), 2, 17, 12, 8, want.shape[1],
+                                          want.shape[2], 0.05, -128, 127, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    assert_equal(yf, want, "maxpool f32")
+    assert_equal(yq, orc.quantize(want, 0.05, -128, 127), "maxpool codes")
