@@ -100,9 +100,9 @@ typedef struct {
 W4A8_API int w4a8_gemm(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int w_kind, int M, int N, int K,
               const w4a8_epilogue* epi, void* C, int64_t ldc, void* stream);
 
-/* Convolution geometry. Input is int8 NHWC [n, h, w, c] with c == 16, c a
- * multiple of 32 up to 128, or c a multiple of 128 (pad channels with zero
- * codes and zero weights otherwise).
+/* Convolution geometry. Input is int8 NHWC [n, h, w, c] with c in
+ * {16, 32, 64} or c a multiple of 128 (pad channels with zero codes and
+ * zero weights otherwise); c == 16 only at stride 1.
  * Weights are [o, groups, kh*kw, c/groups_of_128] in the w_kind encoding:
  * for c <= 128 that is OHWI ([o][kh][kw][c]); for c > 128 channels are
  * split in groups of 128 and the group index is outermost. Row stride ldw

@@ -159,6 +159,8 @@ extern "C" int w4a8_gemm(const int8_t* A, int64_t lda, const void* W, int64_t ld
   p.err = device_error_word();
   if (!p.err) return W4A8_ERR_LAUNCH;
   fill_epi(p.epi, epi, C, N);
+  // |acc| <= K * 128 * max|w|; below 2^22 the epilogue skips its range check.
+  p.epi.acc_fits_22 = (double)K * 128.0 * (i4 ? 8.0 : 128.0) < 4194304.0;
   p.epi.s_img = 0;
   p.epi.s_pix = ldc;
   p.epi.s_ch = 1;
@@ -193,8 +195,9 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
     return W4A8_ERR_ARG;
   if (g->stride != 1 && g->stride != 2) return W4A8_ERR_UNSUPPORTED;
   if (g->c % 16) return W4A8_ERR_ALIGN;
-  // A 32-byte MMA K-step must read one tap (or, for c == 16, a tap pair).
-  if (g->c != 16 && (g->c % 32 || (g->c > 128 && g->c % 128))) return W4A8_ERR_UNSUPPORTED;
+  // Halo pixels are 16/32/64/128-byte rows (swizzle widths); wider inputs
+  // are split into groups of 128 channels.
+  if (g->c != 16 && g->c != 32 && g->c != 64 && g->c % 128) return W4A8_ERR_UNSUPPORTED;
   if (g->out_layout != W4A8_LAYOUT_NHWC && g->out_layout != W4A8_LAYOUT_NCHW) return W4A8_ERR_ARG;
   if (g->out_layout == W4A8_LAYOUT_NHWC && g->ldo < g->o) return W4A8_ERR_ARG;
   if (g->pool != 0 && g->pool != 1) return W4A8_ERR_ARG;
@@ -212,9 +215,10 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   if ((long long)(g->ho - 1) * s - g->pad_h >= g->h || (long long)(g->wo - 1) * s - g->pad_w >= g->w)
     return W4A8_ERR_ARG;
 
+  // Halo pixels are stored channel-group-major like NHWC: one pixel = cg
+  // bytes, 128/64/32-byte rows swizzled to match (16-byte rows unswizzled).
   const int cg = g->c < 128 ? g->c : 128;
   const int groups = g->c / cg;
-  const int planes = cg / 16;
   const int kbpg = (taps * cg + kBK - 1) / kBK;
   const int steps = kbpg * (kBK / 32);
   if (steps > kMaxSteps) return W4A8_ERR_UNSUPPORTED;
@@ -254,12 +258,12 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
     cp.tiles_h = (g->ho + kTileH - 1) / kTileH;
     cp.tiles_w = (g->wo + kTileW - 1) / kTileW;
   }
-  cp.planes = planes;
+  cp.cg = cg;
+  cp.a_layout = cg == 128 ? kLayoutSw128 : cg == 64 ? kLayoutSw64 : cg == 32 ? kLayoutSw32 : kLayoutNone;
   cp.halo_w = kTileW + span_w;
   cp.halo_h = kTileH + span_h;
   if (cp.halo_w > 256 || cp.halo_h > 256) return W4A8_ERR_UNSUPPORTED;
-  cp.plane_bytes = (uint32_t(cp.halo_w * cp.halo_h * 16) + 127u) & ~127u;
-  cp.slot_bytes = cp.plane_bytes * planes;
+  cp.slot_bytes = (uint32_t(cp.halo_w * cp.halo_h * cg) + 1023u) & ~1023u;
   int slot_of[2][2] = {{-1, -1}, {-1, -1}};
   int slot_py[4], slot_px[4];
   int ns = 0;
@@ -275,17 +279,17 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
       }
   cp.n_slots = ns;
   cp.halo_bytes = (cp.slot_bytes * ns + 1023u) & ~1023u;
-  cp.halo_tx_bytes = uint32_t(ns * planes * cp.halo_w * cp.halo_h * 16);
+  cp.halo_tx_bytes = uint32_t(ns * cp.halo_w * cp.halo_h * cg);
   cp.kb_per_group = kbpg;
   auto chunk_off = [&](int k) -> long long {
-    const int t = k / cg, c = (k % cg) / 16;
+    const int t = k / cg, within = k % cg;
     const int ky = t / g->kw, kx = t % g->kw;
     const int dy = ky - g->pad_h, dx = kx - g->pad_w;
     const int qy = floordiv(dy, s), py = dy - qy * s;
     const int qx = floordiv(dx, s), px = dx - qx * s;
     const int sl = slot_of[py][px];
     const int pix = (qy - qmin_h[py]) * cp.halo_w + (qx - qmin_w[px]);
-    return (long long)sl * cp.slot_bytes + (long long)c * cp.plane_bytes + (long long)pix * 16;
+    return (long long)sl * cp.slot_bytes + (long long)pix * cg + within;
   };
   for (int j = 0; j < steps; ++j) {
     const int k = 32 * j;
@@ -346,6 +350,7 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   p.err = device_error_word();
   if (!p.err) return W4A8_ERR_LAUNCH;
   fill_epi(p.epi, epi, out, g->o);
+  p.epi.acc_fits_22 = (double)k_total * 128.0 * (i4 ? 8.0 : 128.0) < 4194304.0;
   if (g->out_layout == W4A8_LAYOUT_NHWC) {
     p.epi.s_img = (long long)g->ho * g->wo * g->ldo;
     p.epi.s_pix = g->ldo;
@@ -366,14 +371,20 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
     if (encode_u8(&tW, W, 2, dims, str, box, i4 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B))
       return W4A8_ERR_TENSORMAP;
   }
+  const CUtensorMapSwizzle swz = cg == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                 : cg == 64  ? CU_TENSOR_MAP_SWIZZLE_64B
+                                 : cg == 32  ? CU_TENSOR_MAP_SWIZZLE_32B
+                                             : CU_TENSOR_MAP_SWIZZLE_NONE;
   for (int sl = 0; sl < ns; ++sl) {
     const int py = slot_py[sl], px = slot_px[sl];
     const int8_t* base = x + ((long long)py * g->w + px) * g->c;
-    const uint64_t dims[5] = {16, uint64_t(g->c / 16), uint64_t((g->w - px + s - 1) / s),
+    // (channels of the group, group, W, H, N); stride phases double W/H strides.
+    const uint64_t dims[5] = {uint64_t(cg), uint64_t(groups), uint64_t((g->w - px + s - 1) / s),
                               uint64_t((g->h - py + s - 1) / s), uint64_t(g->n)};
-    const uint64_t str[4] = {16, uint64_t(s) * g->c, uint64_t(s) * g->w * g->c, uint64_t(g->h) * g->w * g->c};
-    const uint32_t box[5] = {16, 1, uint32_t(cp.halo_w), uint32_t(cp.halo_h), 1};
-    if (encode_u8(&tH[sl], base, 5, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)) return W4A8_ERR_TENSORMAP;
+    const uint64_t str[4] = {uint64_t(cg), uint64_t(s) * g->c, uint64_t(s) * g->w * g->c,
+                             uint64_t(g->h) * g->w * g->c};
+    const uint32_t box[5] = {uint32_t(cg), 1, uint32_t(cp.halo_w), uint32_t(cp.halo_h), 1};
+    if (encode_u8(&tH[sl], base, 5, dims, str, box, swz)) return W4A8_ERR_TENSORMAP;
   }
   const int grid = std::min(p.tiles_m * p.tiles_n, sms);
   return launch(i4, true, bn, tA, tW, tH, p, grid, static_cast<cudaStream_t>(stream));

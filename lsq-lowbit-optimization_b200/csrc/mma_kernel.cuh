@@ -63,16 +63,17 @@ struct EpiParams {
   long long aux_ld;
   long long s_img, s_pix, s_ch;  // output element strides
   int n_total;                   // valid columns
+  int acc_fits_22;               // host-proven |acc| < 2^22: no per-value range check
 };
 
 struct ConvParams {
   int ho, wo;              // output size
   int tiles_h, tiles_w;    // tiles per image
   int n_slots;             // halo sub-tiles (stride phases) in use
-  int planes;              // 16-byte channel planes per group
+  int cg;                  // channel-group width in bytes (16, 32, 64 or 128) = halo pixel pitch
+  uint32_t a_layout;       // operand layout of the halo: swizzle matching cg (none for 16)
   int halo_w, halo_h;      // sub-halo size in pixels
-  uint32_t plane_bytes;    // bytes per plane (128-aligned)
-  uint32_t slot_bytes;     // planes * plane_bytes
+  uint32_t slot_bytes;     // bytes per sub-halo (1024-aligned)
   uint32_t halo_bytes;     // 1024-aligned bytes per halo stage
   uint32_t halo_tx_bytes;  // bytes the TMA loads of one stage deliver
   int slot_qh[4], slot_qw[4];  // per slot: TMA start offset in phase-view units
@@ -138,7 +139,139 @@ __device__ __forceinline__ float lsq_guard(float y, float t, float s) {
 
 struct EpiConsts {
   float rs, qnf, qpf;
+  bool relu_in_clamp;  // s8 output, qn >= 0, no float32 side output: the clamp is the ReLU
 };
+
+// Packed float32 pairs (add/mul.rn.f32x2: two independent IEEE round-to-
+// nearest operations, bit-identical to the scalar forms).
+__device__ __forceinline__ uint64_t fpair(float lo, float hi) {
+  return uint64_t(__float_as_uint(lo)) | (uint64_t(__float_as_uint(hi)) << 32);
+}
+__device__ __forceinline__ float flo(uint64_t v) { return __uint_as_float(uint32_t(v)); }
+__device__ __forceinline__ float fhi(uint64_t v) { return __uint_as_float(uint32_t(v >> 32)); }
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// Common-case epilogue for 16 contiguous columns (aligned vectors, NHWC /
+// row-major output): the same arithmetic as epilogue16, on float pairs.
+__device__ __forceinline__ void epilogue16_fast(const EpiParams& e, const EpiConsts& k, const uint32_t* acc, int n,
+                                                long long out_off, long long prow) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const uint64_t magic2 = fpair(kMagic, kMagic), neg_magic2 = fpair(-kMagic, -kMagic);
+  uint64_t y[8];
+  bool small = e.acc_fits_22 != 0;
+  if (!small) {
+    uint32_t oor = 0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) oor |= (acc[i] + 0x400000u) & 0xFF800000u;
+    small = oor == 0;
+  }
+  if (small) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      y[j] = add2(uint64_t(acc[2 * j] + 0x4B400000u) | (uint64_t(acc[2 * j + 1] + 0x4B400000u) << 32), neg_magic2);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = fpair(__int2float_rn(int(acc[2 * j])), __int2float_rn(int(acc[2 * j + 1])));
+  }
+  if (e.alpha) {
+    const ulonglong2* a2 = reinterpret_cast<const ulonglong2*>(e.alpha + n);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const ulonglong2 v = __ldg(a2 + g);
+      y[2 * g] = mul2(y[2 * g], v.x);
+      y[2 * g + 1] = mul2(y[2 * g + 1], v.y);
+    }
+  } else {
+    const uint64_t a = fpair(e.alpha_scalar, e.alpha_scalar);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = mul2(y[j], a);
+  }
+  if (e.beta) {
+    const ulonglong2* b2 = reinterpret_cast<const ulonglong2*>(e.beta + n);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const ulonglong2 v = __ldg(b2 + g);
+      y[2 * g] = add2(y[2 * g], v.x);
+      y[2 * g + 1] = add2(y[2 * g + 1], v.y);
+    }
+  }
+  if (e.residual) {
+    const ulonglong2* r2 = reinterpret_cast<const ulonglong2*>(e.residual + prow * e.res_ld + n);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const ulonglong2 v = r2[g];
+      y[2 * g] = add2(y[2 * g], v.x);
+      y[2 * g + 1] = add2(y[2 * g + 1], v.y);
+    }
+  }
+  if (e.relu && !k.relu_in_clamp) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = fpair(fmaxf(flo(y[j]), 0.0f), fmaxf(fhi(y[j]), 0.0f));
+  }
+  if (e.aux) {
+    ulonglong2* d2 = reinterpret_cast<ulonglong2*>(e.aux + prow * e.aux_ld + n);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) d2[g] = make_ulonglong2(y[2 * g], y[2 * g + 1]);
+  }
+  if (e.out_kind == 1) {
+    ulonglong2* d2 = reinterpret_cast<ulonglong2*>(static_cast<float*>(e.out) + out_off);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) d2[g] = make_ulonglong2(y[2 * g], y[2 * g + 1]);
+    return;
+  }
+  if (e.out_kind == 2) {
+    uint32_t w[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      w[j] = uint32_t(__half_as_ushort(__float2half_rn(flo(y[j])))) |
+             (uint32_t(__half_as_ushort(__float2half_rn(fhi(y[j])))) << 16);
+    uint4* d4 = reinterpret_cast<uint4*>(static_cast<__half*>(e.out) + out_off);
+    d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    return;
+  }
+  // LSQ codes: t = y * fl(1/s); guard band -> exact quotient (see lsq_code);
+  // clamp; the low byte of the 1.5*2^23-biased float is the int8 code.
+  const uint64_t rs2 = fpair(k.rs, k.rs);
+  uint64_t t[8];
+  bool slow = false;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    t[j] = mul2(y[j], rs2);
+    const uint64_t rt = add2(add2(t[j], magic2), neg_magic2);
+    const uint64_t d = add2(t[j], rt ^ 0x8000000080000000ull);  // t - rint(t)
+    slow |= (fabsf(flo(t[j])) < 256.0f) & (fabsf(flo(d)) > 0.49975586f);
+    slow |= (fabsf(fhi(t[j])) < 256.0f) & (fabsf(fhi(d)) > 0.49975586f);
+  }
+  if (slow) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      t[j] = fpair(lsq_guard(flo(y[j]), flo(t[j]), e.out_scale), lsq_guard(fhi(y[j]), fhi(t[j]), e.out_scale));
+  }
+  uint32_t b[16];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint64_t c = add2(fpair(fminf(fmaxf(flo(t[j]), k.qnf), k.qpf), fminf(fmaxf(fhi(t[j]), k.qnf), k.qpf)),
+                            magic2);
+    b[2 * j] = uint32_t(c);
+    b[2 * j + 1] = uint32_t(c >> 32);
+  }
+  uint4 w;
+  w.x = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+  w.y = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
+  w.z = __byte_perm(__byte_perm(b[8], b[9], 0x0040), __byte_perm(b[10], b[11], 0x0040), 0x5410);
+  w.w = __byte_perm(__byte_perm(b[12], b[13], 0x0040), __byte_perm(b[14], b[15], 0x0040), 0x5410);
+  *reinterpret_cast<uint4*>(static_cast<int8_t*>(e.out) + out_off) = w;
+}
 
 // Applies the fused epilogue to 16 accumulators (columns n .. n+15) of one
 // output row; all indexing is static so nothing spills to local memory.
@@ -147,6 +280,18 @@ __device__ __forceinline__ void epilogue16(const EpiParams& e, const EpiConsts& 
   const int ncols = min(16, e.n_total - n);
   if (ncols <= 0) return;
   const bool vec = (ncols == 16) && (e.s_ch == 1);
+  if (vec && e.out_kind != 0) {
+    const size_t esz = e.out_kind == 1 ? 4 : (e.out_kind == 2 ? 2 : 1);
+    const uintptr_t mis =
+        (reinterpret_cast<uintptr_t>(static_cast<const char*>(e.out) + out_off * esz)) |
+        (e.alpha ? reinterpret_cast<uintptr_t>(e.alpha + n) : 0) | (e.beta ? reinterpret_cast<uintptr_t>(e.beta + n) : 0) |
+        (e.residual ? reinterpret_cast<uintptr_t>(e.residual + prow * e.res_ld + n) : 0) |
+        (e.aux ? reinterpret_cast<uintptr_t>(e.aux + prow * e.aux_ld + n) : 0);
+    if ((mis & 15) == 0) {
+      epilogue16_fast(e, k, acc, n, out_off, prow);
+      return;
+    }
+  }
   if (e.out_kind == 0) {
     int32_t* dst = static_cast<int32_t*>(e.out) + out_off;
     if (vec && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
@@ -510,9 +655,8 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
               uint8_t* hdst = base + p.h_off + hs * p.conv.halo_bytes;
               for (int sl = 0; sl < p.conv.n_slots; ++sl) {
                 const CUtensorMap* m = sl == 0 ? &tmH0 : sl == 1 ? &tmH1 : sl == 2 ? &tmH2 : &tmH3;
-                for (int pl = 0; pl < p.conv.planes; ++pl)
-                  tma_load_5d(hdst + sl * p.conv.slot_bytes + pl * p.conv.plane_bytes, m, &bar_hfull[hs], 0,
-                              g * p.conv.planes + pl, ow0 + p.conv.slot_qw[sl], oh0 + p.conv.slot_qh[sl], img);
+                tma_load_5d(hdst + sl * p.conv.slot_bytes, m, &bar_hfull[hs], 0, g, ow0 + p.conv.slot_qw[sl],
+                            oh0 + p.conv.slot_qh[sl], img);
               }
               if (++hs == p.halo_stages) { hs = 0; hph ^= 1; }
             }
@@ -589,8 +733,10 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
             uint64_t a_desc;
             if constexpr (kConv) {
               const int step = kb_in_g * 4 + j;
-              a_desc = make_smem_desc(halo_addr + p.conv.step_off[step], p.conv.step_lbo[step],
-                                      p.conv.halo_w * 16, kLayoutNone);
+              const uint32_t a_addr = halo_addr + p.conv.step_off[step];
+              // The swizzle phase follows the absolute smem address (as the TMA
+              // wrote it), so a tap starting mid-pattern needs base offset 0.
+              a_desc = make_smem_desc(a_addr, p.conv.step_lbo[step], p.conv.halo_w * p.conv.cg, p.conv.a_layout);
             } else {
               a_desc = make_smem_desc(base_u32 + p.a_off + s * p.a_stage_bytes + j * 32, 16, 1024, kLayoutSw128);
             }
@@ -626,6 +772,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
     k.rs = p.epi.out_kind == 3 ? __frcp_rn(p.epi.out_scale) : 1.0f;
     k.qnf = float(p.epi.qn);
     k.qpf = float(p.epi.qp);
+    k.relu_in_clamp = p.epi.out_kind == 3 && p.epi.qn >= 0 && p.epi.aux == nullptr;
     int it = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
       const int buf = it & 1;

@@ -187,14 +187,19 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 // at [61,64): 0 = no swizzle (8x16B core matrices), 2 = 128B swizzle.
 constexpr uint32_t kLayoutNone = 0;
 constexpr uint32_t kLayoutSw128 = 2;
+constexpr uint32_t kLayoutSw64 = 4;
+constexpr uint32_t kLayoutSw32 = 6;
 
+// base_offset [49,52) stays 0 here: the swizzle pattern is taken from the
+// absolute shared-memory address bits, the same bits the TMA swizzled by.
 __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
-                                                   uint32_t layout) {
+                                                   uint32_t layout, uint32_t base_offset = 0) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= 1ull << 46;
+  d |= static_cast<uint64_t>(base_offset & 7u) << 49;
   d |= static_cast<uint64_t>(layout & 7u) << 61;
   return d;
 }

@@ -221,12 +221,15 @@ def repack_oihw_int4(w_packed: torch.Tensor, c: int, kh: int, kw: int, c_pad: in
 
 
 def conv_channels_padded(c: int, stride: int = 1) -> int:
-    """Channel count the conv kernel accepts: 16 (stride 1 only), a multiple
-    of 32 up to 128, or a multiple of 128. A 32-byte MMA K-step must read
-    one tap, or for 16 channels two taps of one stride phase."""
+    """Channel count the conv kernel accepts: 16 (stride 1 only), 32, 64 or
+    a multiple of 128 — the halo stores one pixel per 16/32/64/128-byte
+    swizzled row."""
     if c <= 16 and stride == 1:
         return 16
-    return _round_up(c, 32) if c <= 128 else _round_up(c, 128)
+    for width in (32, 64):
+        if c <= width:
+            return width
+    return _round_up(c, 128)
 
 
 # ---------------------------------------------------------------------------

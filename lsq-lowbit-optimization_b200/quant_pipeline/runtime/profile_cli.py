@@ -57,7 +57,12 @@ def conv(a) -> dict:
     if a.residual:
         res = torch.randn((a.n, ho, ho, a.o), device=dev, generator=g)
         aux = torch.empty_like(res)
-    geom = ext.ConvGeom(a.n, a.h, a.h, a.c, a.k, a.k, a.stride, a.pad, a.pad, ho, ho, a.o, ext.LAYOUT_NHWC, a.o)
+    if a.pool:
+        ph = (ho - 1) // 2 + 1
+        out = torch.empty((a.n, ph, ph, a.o), dtype=out.dtype, device=dev)
+        aux = torch.empty((a.n, ph, ph, a.o), dtype=torch.float32, device=dev)
+    geom = ext.ConvGeom(a.n, a.h, a.h, a.c, a.k, a.k, a.stride, a.pad, a.pad, ho, ho, a.o, ext.LAYOUT_NHWC, a.o,
+                        int(a.pool))
     epi = ext.make_epilogue(kind, alpha=alpha, beta=beta, relu=True, out_scale=0.05, qn=0, qp=127,
                             residual=res, res_ld=a.o, aux=aux, aux_ld=a.o)
     wkind = ext.W_INT4 if a.wbits == 4 else ext.W_INT8
@@ -107,6 +112,7 @@ def main() -> None:
         c.add_argument(f"--{k}", type=int, default=v)
     c.add_argument("--out", choices=["s8", "f32"], default="s8")
     c.add_argument("--residual", action="store_true")
+    c.add_argument("--pool", action="store_true", help="fuse the 3x3/s2/p1 max pool (float32 side output)")
     gm = sub.add_parser("gemm")
     for k, v in dict(m=4096, n=8192, k=8192, wbits=4).items():
         gm.add_argument(f"--{k}", type=int, default=v)

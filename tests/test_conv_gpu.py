@@ -57,7 +57,8 @@ CONV_CASES = [
     (2, 56, 56, 64, 128, 1, 2, 0),
     (2, 14, 14, 256, 512, 1, 2, 0),
     (2, 9, 13, 32, 48, 1, 1, 0),
-    (2, 11, 9, 96, 80, 3, 1, 1),
+    (2, 11, 9, 32, 80, 3, 1, 1),
+    (2, 9, 9, 384, 64, 3, 2, 1),
 ]
 
 
@@ -74,10 +75,10 @@ def test_conv_nhwc_s32_bitexact(cuda, n, h, w, c, o, k, stride, pad):
     assert ext.device_error() == 0
 
 
-@pytest.mark.parametrize("c,stride", [(48, 1), (16, 2)])
+@pytest.mark.parametrize("c,stride", [(48, 1), (96, 1), (16, 2)])
 def test_conv_channel_rule(cuda, c, stride):
-    """c = 48, or c = 16 at stride 2, would split a 32-byte K-step across
-    taps or stride phases: rejected on the host, not miscomputed."""
+    """c = 48 or 96 is not a halo row width, c = 16 at stride 2 would split a
+    32-byte K-step across stride phases: rejected on the host."""
     g = rng(9)
     xq = rand_i8(g, (1, 8, 8, c), 0, 127)
     wt = rand_i4(g, (16, 3, 3, c))

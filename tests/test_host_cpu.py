@@ -80,6 +80,7 @@ def test_conv_channel_padding_rule():
 
     assert ext.conv_channels_padded(3) == 16 and ext.conv_channels_padded(3, 2) == 32
     assert ext.conv_channels_padded(48) == 64 and ext.conv_channels_padded(130) == 256
+    assert ext.conv_channels_padded(96) == 128 and ext.conv_channels_padded(20) == 32
     assert ext.conv_channels_padded(512) == 512
 
 
