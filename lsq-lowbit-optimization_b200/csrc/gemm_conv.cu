@@ -321,8 +321,9 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   // at least two halo stages, the CTA loads and unpacks the weights once and
   // then streams only input halos.
   const uint32_t bres_bytes = uint32_t(p.num_kb) * per_stage;
-  // The fused pool stages one tile of int32 accumulators (128 x 68 words).
-  const uint32_t pool_bytes = g->pool ? uint32_t(kBM * kPoolPitch * 4 + 1023) & ~1023u : 0u;
+  // The fused pool stages one tile of int32 accumulators (128 x 68 words)
+  // per epilogue warp set.
+  const uint32_t pool_bytes = g->pool ? uint32_t(acc_buffers(bn, true)) * kPoolStageBytes : 0u;
   const int budget = kSmemBudget - int(pool_bytes);
   p.b_resident = 0;
   if (p.tiles_n == 1 && bres_bytes + 2 * cp.halo_bytes <= uint32_t(budget)) {

@@ -39,6 +39,23 @@ struct Roles {
   static constexpr int kUnpackWarp0 = 4 + kEpiWarps;
   static constexpr int kThreads = (kUnpackWarp0 + kUnpackWarps) * 32;
 };
+
+// TMEM accumulator buffers (tiles in flight between the MMA and the
+// epilogue): as many as TMEM (512 columns) and the epilogue warp sets (one
+// set of >= 4 warps per buffer) allow, at most 4. Each epilogue warp set
+// drains one buffer, so short-K tiles overlap their epilogues.
+__host__ __device__ constexpr int acc_buffers(int bn, bool conv) {
+  const int by_warps = (conv ? Roles<true>::kEpiWarps : Roles<false>::kEpiWarps) / 4;
+  const int by_tmem = 512 / bn;
+  const int nb = by_warps < by_tmem ? by_warps : by_tmem;
+  return nb < 4 ? nb : 4;
+}
+__host__ __device__ constexpr uint32_t tmem_columns(int bn, bool conv) {
+  const uint32_t need = uint32_t(acc_buffers(bn, conv) * bn);
+  uint32_t cols = 32;
+  while (cols < need) cols <<= 1;
+  return cols;
+}
 constexpr int kMaxStages = 8;
 constexpr int kMaxHaloStages = 6;
 constexpr int kMaxSteps = 64;     // conv MMA K-steps (32 B) per channel group
@@ -47,6 +64,7 @@ constexpr int kTileW = 8;         // conv: output columns per tile
 // Fused max pool: a 16x8 conv tile at origin (14*th - 1, 6*tw - 1) holds
 // every 3x3/s2 window of a 7x3 block of pooled outputs.
 constexpr int kPoolRows = 7, kPoolCols = 3, kPoolPitch = 68;  // staging row pitch (int32)
+constexpr uint32_t kPoolStageBytes = 128 * kPoolPitch * 4;     // one staging tile (34 KB, 1 KB multiple)
 
 struct EpiParams {
   void* out;
@@ -471,10 +489,10 @@ __device__ __forceinline__ bool row_coords(const KParams& p, int mt, int m, long
 // min (the epilogue is increasing in acc where alpha >= 0, decreasing where
 // alpha < 0), applies the epilogue to the selected accumulator and stores
 // the pooled codes (out) and float32 values (aux).
-template <int BN, int kEpiWarps>
+template <int BN, int kSetWarps>
 __device__ __forceinline__ void pool_epilogue(const KParams& p, const EpiConsts& k, uint32_t t_addr,
                                               uint8_t* stage_bytes, int mt, int m, int slice, int slices, int ew,
-                                              int lane, uint64_t* tempty) {
+                                              int lane, uint64_t* tempty, int bar_id) {
   int32_t* stg = reinterpret_cast<int32_t*>(stage_bytes);
   for (int c0 = slice * (BN / slices); c0 < (slice + 1) * (BN / slices); c0 += 16) {
     uint32_t acc[16];
@@ -487,7 +505,7 @@ __device__ __forceinline__ void pool_epilogue(const KParams& p, const EpiConsts&
   }
   tc_fence_before();
   mbar_arrive(tempty);
-  bar_sync(2, kEpiWarps * 32);
+  bar_sync(bar_id, kSetWarps * 32);
   const ConvParams& c = p.conv;
   const EpiParams& e = p.epi;
   const int per_img = c.tiles_h * c.tiles_w;
@@ -497,8 +515,7 @@ __device__ __forceinline__ void pool_epilogue(const KParams& p, const EpiConsts&
   const int tw = rem - th * c.tiles_w;
   const int oh0 = th * 2 * kPoolRows - 1, ow0 = tw * 2 * kPoolCols - 1;
   constexpr int kQuads = BN / 4;
-  const int w = ew * 32 + lane;
-  if (w < kPoolRows * kPoolCols * kQuads) {
+  for (int w = ew * 32 + lane; w < kPoolRows * kPoolCols * kQuads; w += kSetWarps * 32) {
     const int pix = w / kQuads, quad = w - pix * kQuads;
     const int pr_l = pix / kPoolCols, pc_l = pix - pr_l * kPoolCols;
     const int pr = th * kPoolRows + pr_l, pc = tw * kPoolCols + pc_l;
@@ -542,7 +559,7 @@ __device__ __forceinline__ void pool_epilogue(const KParams& p, const EpiConsts&
       }
     }
   }
-  bar_sync(2, kEpiWarps * 32);  // the staging tile is free for the next tile
+  bar_sync(bar_id, kSetWarps * 32);  // the staging tile is free for the next tile
 }
 
 // ------------------------------ kernel -------------------------------------
@@ -555,15 +572,18 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
   constexpr int kEpiWarps = Roles<kConv>::kEpiWarps;
   constexpr int kUnpackWarp0 = Roles<kConv>::kUnpackWarp0;
   constexpr int kUnpackThreads = Roles<kConv>::kUnpackWarps * 32;
-  constexpr int kSlices = kEpiWarps / 4;  // column slices per TMEM lane quadrant
+  constexpr int kNB = acc_buffers(BN, kConv);        // accumulator buffers = epilogue warp sets
+  constexpr int kSetWarps = kEpiWarps / kNB;         // warps per set (a multiple of 4)
+  constexpr int kSlices = kSetWarps / 4;             // column slices per TMEM lane quadrant
+  constexpr uint32_t kTmemCols = tmem_columns(BN, kConv);
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_full[kMaxStages];
   __shared__ __align__(8) uint64_t bar_ready[kMaxStages];
   __shared__ __align__(8) uint64_t bar_empty[kMaxStages];
   __shared__ __align__(8) uint64_t bar_hfull[kMaxHaloStages];
   __shared__ __align__(8) uint64_t bar_hempty[kMaxHaloStages];
-  __shared__ __align__(8) uint64_t bar_tfull[2];
-  __shared__ __align__(8) uint64_t bar_tempty[2];
+  __shared__ __align__(8) uint64_t bar_tfull[4];
+  __shared__ __align__(8) uint64_t bar_tempty[4];
   __shared__ __align__(8) uint64_t bar_drain;
   __shared__ __align__(8) uint64_t bar_bres;    // resident weights landed
   __shared__ __align__(8) uint64_t bar_bready;  // resident weights unpacked
@@ -585,9 +605,9 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       mbar_init(&bar_hfull[s], 1);
       mbar_init(&bar_hempty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kNB; ++b) {
       mbar_init(&bar_tfull[b], 1);
-      mbar_init(&bar_tempty[b], kEpiWarps * 32);
+      mbar_init(&bar_tempty[b], kSetWarps * 32);
     }
     mbar_init(&bar_drain, 1);
     mbar_init(&bar_bres, 1);
@@ -606,7 +626,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
     fence_proxy_async_smem();
   }
   if (warp == 1) {
-    tmem_alloc(&tmem_slot, p.tmem_cols);
+    tmem_alloc(&tmem_slot, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -710,8 +730,8 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       const bool resident = kConv && p.b_resident;
       if (resident) ok = mbar_wait(kInt4 ? &bar_bready : &bar_bres, 0, &abort_flag);
       for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x, ++it) {
-        const int buf = it & 1;
-        if (!mbar_wait(&bar_tempty[buf], ((it >> 1) & 1) ^ 1, &abort_flag)) { ok = false; break; }
+        const int buf = it % kNB;
+        if (!mbar_wait(&bar_tempty[buf], ((it / kNB) & 1) ^ 1, &abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         uint32_t halo_addr = 0;
@@ -766,18 +786,19 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
   } else if (warp >= 4 && warp < 4 + kEpiWarps) {
     // ----------------------------- epilogue --------------------------------
     const int q = warp & 3;
-    const int slice = (warp - 4) >> 2;
+    const int set = (warp - 4) / kSetWarps;          // this warp drains buffer `set`
+    const int slice = ((warp - 4) % kSetWarps) >> 2;
     const int m = q * 32 + lane;
     EpiConsts k;
     k.rs = p.epi.out_kind == 3 ? __frcp_rn(p.epi.out_scale) : 1.0f;
     k.qnf = float(p.epi.qn);
     k.qpf = float(p.epi.qp);
     k.relu_in_clamp = p.epi.out_kind == 3 && p.epi.qn >= 0 && p.epi.aux == nullptr;
-    int it = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++it) {
-      const int buf = it & 1;
+    int it = set;
+    for (int t = blockIdx.x + set * gridDim.x; t < total_tiles; t += kNB * gridDim.x, it += kNB) {
+      const int buf = set;
       int ok = 1;
-      if (lane == 0) ok = mbar_wait(&bar_tfull[buf], (it >> 1) & 1, &abort_flag) ? 1 : 0;
+      if (lane == 0) ok = mbar_wait(&bar_tfull[buf], (it / kNB) & 1, &abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         if (lane == 0) atomicOr(p.err, kErrTimeoutEpilogue);
@@ -787,8 +808,9 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       const int mt = t / p.tiles_n;
       const int nt = t - mt * p.tiles_n;
       if (kConv && p.conv.pool) {
-        pool_epilogue<BN, kEpiWarps>(p, k, tmem_base + (uint32_t(q * 32) << 16) + buf * BN, base + p.conv.pool_off,
-                                     mt, m, slice, kSlices, warp - 4, lane, &bar_tempty[buf]);
+        pool_epilogue<BN, kSetWarps>(p, k, tmem_base + (uint32_t(q * 32) << 16) + buf * BN,
+                                     base + p.conv.pool_off + set * kPoolStageBytes, mt, m, slice, kSlices,
+                                     (warp - 4) % kSetWarps, lane, &bar_tempty[buf], 2 + set);
         continue;
       }
       long long out_off = 0, prow = 0;
@@ -875,7 +897,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, p.tmem_cols);
+    tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
