@@ -291,19 +291,20 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
     const int pix = (qy - qmin_h[py]) * cp.halo_w + (qx - qmin_w[px]);
     return (long long)sl * cp.slot_bytes + (long long)pix * cg + within;
   };
+  // One operand descriptor per 32-byte K-step, relative to the halo stage
+  // base; steps past the real K repeat step 0 (their weights are zero).
+  const uint32_t sbo = uint32_t(cp.halo_w * cg);
   for (int j = 0; j < steps; ++j) {
     const int k = 32 * j;
     if (k >= taps * cg) {
-      cp.step_off[j] = cp.step_off[0];
-      cp.step_lbo[j] = cp.step_lbo[0];
+      cp.step_desc[j] = cp.step_desc[0];
       continue;
     }
     const long long o1 = chunk_off(k);
     long long lbo = 16;
     if (k + 16 < taps * cg) lbo = chunk_off(k + 16) - o1;
-    if (lbo <= 0 || (lbo % 16) || lbo >= (1 << 18)) return W4A8_ERR_UNSUPPORTED;
-    cp.step_off[j] = uint32_t(o1);
-    cp.step_lbo[j] = uint32_t(lbo);
+    if (lbo <= 0 || (lbo % 16) || lbo >= (1 << 18) || o1 >= (1 << 18)) return W4A8_ERR_UNSUPPORTED;
+    cp.step_desc[j] = make_smem_desc(uint32_t(o1), uint32_t(lbo), sbo, cp.a_layout);
   }
 
   const int sms = device_sms();

@@ -99,8 +99,9 @@ struct ConvParams {
   int pool;                // 1: fused 3x3/s2/p1 max pool (tiles overlap by one row/column)
   int pho, pwo;            // pooled output size
   uint32_t pool_off;       // smem offset of the int32 accumulator staging tile
-  uint32_t step_off[kMaxSteps];  // smem byte offset of the first 16 B K-chunk
-  uint32_t step_lbo[kMaxSteps];  // byte distance to the second 16 B K-chunk
+  // A-operand descriptor of each 32-byte K-step relative to the halo stage
+  // base (start address = offset inside the stage; add stage_addr >> 4).
+  uint64_t step_desc[kMaxSteps];
 };
 
 struct KParams {
@@ -724,6 +725,12 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
     // ------------------------------ MMA ------------------------------------
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_i8(kBM, BN);
+      // Descriptor templates (start address 0): the issue loop only adds the
+      // stage / halo base, keeping this single thread's per-MMA work short
+      // enough to keep the tensor core fed.
+      const uint64_t sw128_tmpl = make_smem_desc(0, 16, 1024, kLayoutSw128);
+      const uint32_t a_stage0 = (base_u32 + p.a_off) >> 4, b_stage0 = (base_u32 + p.b_off) >> 4;
+      const uint32_t a_step = p.a_stage_bytes >> 4, b_step = p.b_stage_bytes >> 4;
       int s = 0, hs = 0, it = 0;
       uint32_t ph = 0, hph = 0;
       bool ok = true;
@@ -734,35 +741,31 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
         if (!mbar_wait(&bar_tempty[buf], ((it / kNB) & 1) ^ 1, &abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        uint32_t halo_addr = 0;
+        uint32_t halo_lo = 0;
         int kb_in_g = 0;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if constexpr (kConv) {
             if (kb_in_g == 0) {
               if (!mbar_wait(&bar_hfull[hs], hph, &abort_flag)) { ok = false; break; }
-              halo_addr = base_u32 + p.h_off + hs * p.conv.halo_bytes;
+              halo_lo = (base_u32 + p.h_off + hs * p.conv.halo_bytes) >> 4;
             }
           }
           if (!resident) {
             if (!mbar_wait(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag)) { ok = false; break; }
           }
           tc_fence_after();
-          const uint32_t b_addr = base_u32 + p.b_off + (resident ? kb : s) * p.b_stage_bytes;
+          const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(resident ? kb : s) * b_step);
+          uint64_t a_desc[4];
+          if constexpr (kConv) {
 #pragma unroll
-          for (int j = 0; j < kBK / 32; ++j) {
-            uint64_t a_desc;
-            if constexpr (kConv) {
-              const int step = kb_in_g * 4 + j;
-              const uint32_t a_addr = halo_addr + p.conv.step_off[step];
-              // The swizzle phase follows the absolute smem address (as the TMA
-              // wrote it), so a tap starting mid-pattern needs base offset 0.
-              a_desc = make_smem_desc(a_addr, p.conv.step_lbo[step], p.conv.halo_w * p.conv.cg, p.conv.a_layout);
-            } else {
-              a_desc = make_smem_desc(base_u32 + p.a_off + s * p.a_stage_bytes + j * 32, 16, 1024, kLayoutSw128);
-            }
-            const uint64_t b_desc = make_smem_desc(b_addr + j * 32, 16, 1024, kLayoutSw128);
-            mma_i8_ss(d_tmem, a_desc, b_desc, idesc, (kb | j) != 0 ? 1u : 0u);
+            for (int j = 0; j < 4; ++j) a_desc[j] = p.conv.step_desc[kb_in_g * 4 + j] + halo_lo;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) a_desc[j] = sw128_tmpl + (a_stage0 + uint32_t(s) * a_step + 2 * j);
           }
+#pragma unroll
+          for (int j = 0; j < kBK / 32; ++j)
+            mma_i8_ss(d_tmem, a_desc[j], b_desc0 + 2 * j, idesc, (kb | j) != 0 ? 1u : 0u);
           if (!resident) mma_commit(&bar_empty[s]);
           if constexpr (kConv) {
             if (++kb_in_g == kbpg) {

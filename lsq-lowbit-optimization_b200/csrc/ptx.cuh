@@ -192,8 +192,12 @@ constexpr uint32_t kLayoutSw32 = 6;
 
 // base_offset [49,52) stays 0 here: the swizzle pattern is taken from the
 // absolute shared-memory address bits, the same bits the TMA swizzled by.
-__device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
-                                                   uint32_t layout, uint32_t base_offset = 0) {
+// The start-address field holds addr >> 4 in 14 bits; every shared-memory
+// address is below 2^18, so a template built for address 0 becomes the
+// descriptor of address `a` by adding a >> 4 (no carry out of the field).
+// Hot loops add to precomputed templates instead of re-encoding.
+__host__ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                                            uint32_t layout, uint32_t base_offset = 0) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
