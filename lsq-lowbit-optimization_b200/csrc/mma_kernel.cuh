@@ -736,47 +736,59 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       bool ok = true;
       const bool resident = kConv && p.b_resident;
       if (resident) ok = mbar_wait(kInt4 ? &bar_bready : &bar_bres, 0, &abort_flag);
+      // The inner loops carry no break: a failed wait clears `ok` and sets the
+      // CTA's abort flag (so every later wait gives up within a few hundred
+      // polls), the tile's remaining MMAs read in-bounds shared memory, and
+      // the tile loop stops. Inner loops without exits issue markedly faster.
       for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x, ++it) {
         const int buf = it % kNB;
         if (!mbar_wait(&bar_tempty[buf], ((it / kNB) & 1) ^ 1, &abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
-        uint32_t halo_lo = 0;
-        int kb_in_g = 0;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-          if constexpr (kConv) {
-            if (kb_in_g == 0) {
-              if (!mbar_wait(&bar_hfull[hs], hph, &abort_flag)) { ok = false; break; }
-              halo_lo = (base_u32 + p.h_off + hs * p.conv.halo_bytes) >> 4;
+        if constexpr (kConv) {
+          const int groups = p.num_kb / kbpg;
+          int kb = 0;
+          for (int g = 0; g < groups; ++g) {
+            ok &= mbar_wait(&bar_hfull[hs], hph, &abort_flag);
+            tc_fence_after();
+            const uint32_t halo_lo = (base_u32 + p.h_off + hs * p.conv.halo_bytes) >> 4;
+            if (resident) {
+              for (int i = 0; i < kbpg; ++i, ++kb) {
+                const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(kb) * b_step);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  mma_i8_ss(d_tmem, p.conv.step_desc[i * 4 + j] + halo_lo, b_desc0 + 2 * j, idesc,
+                            (kb | j) != 0 ? 1u : 0u);
+              }
+            } else {
+              for (int i = 0; i < kbpg; ++i, ++kb) {
+                ok &= mbar_wait(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag);
+                tc_fence_after();
+                const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(s) * b_step);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  mma_i8_ss(d_tmem, p.conv.step_desc[i * 4 + j] + halo_lo, b_desc0 + 2 * j, idesc,
+                            (kb | j) != 0 ? 1u : 0u);
+                mma_commit(&bar_empty[s]);
+                if (++s == p.stages) { s = 0; ph ^= 1; }
+              }
             }
+            mma_commit(&bar_hempty[hs]);
+            if (++hs == p.halo_stages) { hs = 0; hph ^= 1; }
           }
-          if (!resident) {
-            if (!mbar_wait(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag)) { ok = false; break; }
-          }
-          tc_fence_after();
-          const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(resident ? kb : s) * b_step);
-          uint64_t a_desc[4];
-          if constexpr (kConv) {
+        } else {
+          for (int kb = 0; kb < p.num_kb; ++kb) {
+            ok &= mbar_wait(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag);
+            tc_fence_after();
+            const uint64_t a_desc0 = sw128_tmpl + (a_stage0 + uint32_t(s) * a_step);
+            const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(s) * b_step);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) a_desc[j] = p.conv.step_desc[kb_in_g * 4 + j] + halo_lo;
-          } else {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) a_desc[j] = sw128_tmpl + (a_stage0 + uint32_t(s) * a_step + 2 * j);
+            for (int j = 0; j < 4; ++j)
+              mma_i8_ss(d_tmem, a_desc0 + 2 * j, b_desc0 + 2 * j, idesc, (kb | j) != 0 ? 1u : 0u);
+            mma_commit(&bar_empty[s]);
+            if (++s == p.stages) { s = 0; ph ^= 1; }
           }
-#pragma unroll
-          for (int j = 0; j < kBK / 32; ++j)
-            mma_i8_ss(d_tmem, a_desc[j], b_desc0 + 2 * j, idesc, (kb | j) != 0 ? 1u : 0u);
-          if (!resident) mma_commit(&bar_empty[s]);
-          if constexpr (kConv) {
-            if (++kb_in_g == kbpg) {
-              kb_in_g = 0;
-              mma_commit(&bar_hempty[hs]);
-              if (++hs == p.halo_stages) { hs = 0; hph ^= 1; }
-            }
-          }
-          if (!resident && ++s == p.stages) { s = 0; ph ^= 1; }
         }
-        if (!ok) break;
         mma_commit(&bar_tfull[buf]);
       }
       // Drain: all tcgen05 ops of this thread complete before TMEM is freed.

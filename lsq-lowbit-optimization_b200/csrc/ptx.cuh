@@ -68,10 +68,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity. Returns false (and sets
-// *abort) when the limit passes or another role of the CTA already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
+// Spin part of mbar_wait, kept out of line: an inlined spin loop inside the
+// MMA issue loop slows that loop down even when it is never entered.
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   const unsigned long long t0 = global_timer_ns();
   uint32_t spins = 0;
   while (true) {
@@ -84,6 +83,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       }
     }
   }
+}
+
+// Bounded wait for the phase with the given parity. Returns false (and sets
+// *abort) when the limit passes or another role of the CTA already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, abort_flag);
 }
 
 // AND of `v` over the `count` threads meeting at named barrier `id`; every
