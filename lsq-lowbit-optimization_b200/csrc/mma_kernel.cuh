@@ -573,6 +573,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
   constexpr int kEpiWarps = Roles<kConv>::kEpiWarps;
   constexpr int kUnpackWarp0 = Roles<kConv>::kUnpackWarp0;
   constexpr int kUnpackThreads = Roles<kConv>::kUnpackWarps * 32;
+  constexpr int kUnpackGroups = 2;  // unpack warp groups on alternate k-blocks
   constexpr int kNB = acc_buffers(BN, kConv);        // accumulator buffers = epilogue warp sets
   constexpr int kSetWarps = kEpiWarps / kNB;         // warps per set (a multiple of 4)
   constexpr int kSlices = kSetWarps / 4;             // column slices per TMEM lane quadrant
@@ -599,7 +600,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&bar_full[s], 1);
-      mbar_init(&bar_ready[s], Roles<kConv>::kUnpackWarps);
+      mbar_init(&bar_ready[s], Roles<kConv>::kUnpackWarps / kUnpackGroups);
       mbar_init(&bar_empty[s], 1);
     }
     for (int s = 0; s < p.halo_stages; ++s) {
@@ -846,61 +847,70 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
     }
   } else if (warp >= kUnpackWarp0 && kInt4) {
     // ------------------------------ unpack ---------------------------------
-    // Phase 1 reads every packed chunk this thread owns into registers,
-    // a named barrier orders all reads before any write, phase 2 writes the
-    // int8 rows over the stage (the packed half is overwritten in place).
-    constexpr int kPer = BN * 8 / kUnpackThreads;
+    // kUnpackGroups groups of warps take alternate k-blocks, so one group's
+    // unpack latency (wait, read, expand, write, proxy fence) overlaps the
+    // others'. TMA drops a stage's packed nibbles into the upper half of the
+    // int8 rows they expand to. A group first expands rows [0, BN/2), whose
+    // targets lie below the packed half, then reads the packed bytes of rows
+    // [BN/2, BN), meets at its named barrier (every packed byte of the stage
+    // has now been read) and writes those rows over the packed half.
+    constexpr int kGT = kUnpackThreads / kUnpackGroups;  // threads per group
+    constexpr int kHalf = BN * 4 / kGT;                  // int8 chunks per thread and half
+    static_assert(kGT % 64 == 0 && kHalf >= 1, "unpack group shape");
     const int ut = threadIdx.x - kUnpackWarp0 * 32;
-    // This thread's chunks (row r, 16-byte chunk c of the int8 row) are the
-    // same in every k-block: precompute packed-source and swizzled-target offsets.
-    uint32_t src_off[kPer], dst_off[kPer];
-#pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int idx = ut + kUnpackThreads * j;
-      const int r = idx >> 3, c = idx & 7;
-      src_off[j] = BN * (kBK / 2) + r * 64 + c * 8;
-      dst_off[j] = r * 128 + ((c ^ (r & 7)) << 4);
-    }
-    int s = 0;
-    uint32_t ph = 0;
+    const int ug = ut / kGT, gt = ut % kGT;
+    const uint32_t bar_id = 6 + ug;
+    // Chunk gt + kGT * j is 16-byte chunk (gt & 7) of int8 row (gt >> 3) + j * kGT / 8;
+    // kGT is a multiple of 64, so the swizzle term (row & 7) is the same for all j.
+    const uint32_t src0 = BN * (kBK / 2) + gt * 8;
+    const uint32_t dst0 = (gt >> 3) * 128 + (((gt & 7) ^ ((gt >> 3) & 7)) << 4);
     bool ok = true;
     const bool resident = kConv && p.b_resident;
     // One lane per warp polls the mbarrier (all 32 polling one word
-    // serialises on the shared-memory bank); __syncwarp then orders the
-    // rest of the warp after the observed phase.
+    // serialises on the shared-memory bank); the shuffle orders the rest of
+    // the warp after the observed phase.
     auto wait_warp = [&](uint64_t* bar, uint32_t parity) -> bool {
       int got = 1;
       if (lane == 0) got = mbar_wait(bar, parity, &abort_flag) ? 1 : 0;
       got = __shfl_sync(0xffffffffu, got, 0);
       return got != 0;
     };
-    if (resident) ok = bar_and(1, kUnpackThreads, wait_warp(&bar_bres, 0));
+    if (resident) ok = bar_and(bar_id, kGT, wait_warp(&bar_bres, 0));
     const int passes = resident ? 1 : total_tiles;  // resident weights: one pass over the k-blocks
+    uint32_t q = 0;                                  // k-block sequence number of this CTA
     for (int t = resident ? 0 : int(blockIdx.x); ok && t < passes; t += resident ? 1 : int(gridDim.x)) {
-      for (int kb = 0; kb < p.num_kb; ++kb) {
+      for (int kb = 0; kb < p.num_kb; ++kb, ++q) {
+        if (int(q % kUnpackGroups) != ug) continue;
+        const uint32_t s = resident ? uint32_t(kb) : q % uint32_t(p.stages);
         if (!resident) {
-          if (!bar_and(1, kUnpackThreads, wait_warp(&bar_full[s], ph))) { ok = false; break; }
+          if (!bar_and(bar_id, kGT, wait_warp(&bar_full[s], (q / uint32_t(p.stages)) & 1))) { ok = false; break; }
         }
-        uint8_t* stage = base + p.b_off + (resident ? kb : s) * p.b_stage_bytes;
-        uint2 v[kPer];
+        uint8_t* stage = base + p.b_off + s * p.b_stage_bytes;
+        uint2 v[kHalf];
 #pragma unroll
-        for (int j = 0; j < kPer; ++j) v[j] = *reinterpret_cast<const uint2*>(stage + src_off[j]);
-        bar_sync(1, kUnpackThreads);
+        for (int j = 0; j < kHalf; ++j) v[j] = *reinterpret_cast<const uint2*>(stage + src0 + j * kGT * 8);
 #pragma unroll
-        for (int j = 0; j < kPer; ++j) {
+        for (int j = 0; j < kHalf; ++j) {
           uint4 o;
           unpack_nibbles8(v[j].x, o.x, o.y);
           unpack_nibbles8(v[j].y, o.z, o.w);
-          *reinterpret_cast<uint4*>(stage + dst_off[j]) = o;
+          *reinterpret_cast<uint4*>(stage + dst0 + j * kGT * 16) = o;
+        }
+#pragma unroll
+        for (int j = 0; j < kHalf; ++j)
+          v[j] = *reinterpret_cast<const uint2*>(stage + src0 + (kHalf + j) * kGT * 8);
+        bar_sync(bar_id, kGT);
+#pragma unroll
+        for (int j = 0; j < kHalf; ++j) {
+          uint4 o;
+          unpack_nibbles8(v[j].x, o.x, o.y);
+          unpack_nibbles8(v[j].y, o.z, o.w);
+          *reinterpret_cast<uint4*>(stage + dst0 + (kHalf + j) * kGT * 16) = o;
         }
         fence_proxy_async_smem();
-        if (resident) {
-          bar_sync(1, kUnpackThreads);
-          continue;
-        }
+        if (resident) continue;
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar_ready[s]);
-        if (++s == p.stages) { s = 0; ph ^= 1; }
       }
     }
     __syncwarp();
