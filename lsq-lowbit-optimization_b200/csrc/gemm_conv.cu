@@ -2,6 +2,7 @@
 // argument checks, tile/pipeline sizing, TMA tensor maps, launch.
 #include <algorithm>
 
+#include "gemm_w4_kernel.cuh"
 #include "mma_kernel.cuh"
 #include "tensormap.cuh"
 
@@ -39,6 +40,65 @@ int launch_t(const CUtensorMap& tA, const CUtensorMap& tW, const CUtensorMap* tH
   }
   kern<<<grid, Roles<CV>::kThreads, kSmemAttr, st>>>(tA, tW, tH[0], tH[1], tH[2], tH[3], p);
   return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH;
+}
+
+template <int BN, int CTA>
+int launch_w4_t(const CUtensorMap& tA, const CUtensorMap& tW, const KParams& p, int grid, cudaStream_t st) {
+  auto kern = w4a8_gemm_w4_kernel<BN, CTA>;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAttr) != cudaSuccess)
+      return W4A8_ERR_LAUNCH;
+    if (dev >= 0 && dev < 64) attr_done[dev] = true;
+  }
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(unsigned(grid > 0 ? grid : 2 * 148), 1, 1);
+  cfg.blockDim = dim3(kW4Threads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemAttr;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CTA;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (grid < 0) {  // query: co-resident clusters
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) return 0;
+    return clusters;
+  }
+  if (cudaLaunchKernelEx(&cfg, kern, tA, tW, p) != cudaSuccess) return W4A8_ERR_LAUNCH;
+  return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH;
+}
+
+int launch_w4(int bn, int cta, const CUtensorMap& tA, const CUtensorMap& tW, const KParams& p, int grid,
+              cudaStream_t st) {
+  if (cta == 2) return launch_w4_t<256, 2>(tA, tW, p, grid, st);
+  switch (bn) {
+    case 64: return launch_w4_t<64, 1>(tA, tW, p, grid, st);
+    case 128: return launch_w4_t<128, 1>(tA, tW, p, grid, st);
+    case 256: return launch_w4_t<256, 1>(tA, tW, p, grid, st);
+    default: return W4A8_ERR_UNSUPPORTED;
+  }
+}
+
+// Co-resident CTA pairs of the pair W4 GEMM on the current device (cached).
+int pair_slots() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  CUtensorMap dummy;
+  std::memset(&dummy, 0, sizeof(dummy));
+  KParams p;
+  std::memset(&p, 0, sizeof(p));
+  const int n = launch_w4(256, 2, dummy, dummy, p, -1, nullptr);
+  if (n > 0 && dev >= 0 && dev < 64) cached[dev] = n;
+  return n > 0 ? n : 0;
 }
 
 template <bool I4, bool CV>
@@ -94,6 +154,71 @@ int pick_stages(uint32_t per_stage, uint32_t reserved) {
 
 int floordiv(int a, int b) { return a >= 0 ? a / b : -((-a + b - 1) / b); }
 
+// W4 GEMM on the three-ring kernel; CTA pairs (256 x 256 tiles) when there
+// are enough of them to fill the GPU.
+int gemm_w4(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K,
+            const w4a8_epilogue* epi, void* C, int64_t ldc, int bn, int sms, cudaStream_t stream) {
+  const int pair_tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + 255) / 256);
+  const int slots = (N >= 256 && M > kBM && pair_tiles >= sms / 2) ? pair_slots() : 0;
+  const int cta = slots > 0 ? 2 : 1;
+  if (cta == 2) bn = 256;
+  const int bnl = bn / cta;
+
+  KParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = M;
+  p.N = N;
+  p.num_kb = (K + kBK - 1) / kBK;
+  p.tiles_m = cta == 2 ? (M + 2 * kBM - 1) / (2 * kBM) : (M + kBM - 1) / kBM;
+  p.tiles_n = (N + bn - 1) / bn;
+  // Ring depths: four packed stages (weight bytes arrive far ahead of use),
+  // then A and int8 B stages added in step (A first) while they fit; the
+  // int8 ring covers MMA completion -> unpack -> proxy fence -> arrive.
+  const int64_t a_bytes = kBM * kBK, pk_bytes = int64_t(bnl) * (kBK / 2), b8_bytes = int64_t(bnl) * kBK;
+  int sa = 2, sp = 4, sb = 2;
+  int64_t left = kSmemBudget - sa * a_bytes - sp * pk_bytes - sb * b8_bytes;
+  if (left < 0) return W4A8_ERR_UNSUPPORTED;
+  for (bool grew = true; grew;) {
+    grew = false;
+    if (sa < kMaxStages && left >= a_bytes) { ++sa; left -= a_bytes; grew = true; }
+    if (sb < kMaxB8Stages && left >= b8_bytes) { ++sb; left -= b8_bytes; grew = true; }
+  }
+  while (sp < kMaxPkStages && left >= pk_bytes) { ++sp; left -= pk_bytes; }
+  p.stages = sa;
+  p.pk_stages = sp;
+  p.b8_stages = sb;
+  p.a_off = 0;
+  p.a_stage_bytes = uint32_t(a_bytes);
+  p.bp_off = uint32_t(sa * a_bytes);
+  p.bp_stage_bytes = uint32_t(pk_bytes);
+  p.b_off = uint32_t(p.bp_off + sp * pk_bytes);  // a multiple of 1024 (128-byte swizzle atoms)
+  p.b_stage_bytes = uint32_t(b8_bytes);
+  p.err = device_error_word();
+  if (!p.err) return W4A8_ERR_LAUNCH;
+  fill_epi(p.epi, epi, C, N);
+  p.epi.acc_fits_22 = (double)K * 128.0 * 8.0 < 4194304.0;  // |acc| <= K * 128 * 8
+  p.epi.s_img = 0;
+  p.epi.s_pix = ldc;
+  p.epi.s_ch = 1;
+
+  CUtensorMap tA, tW;
+  {
+    const uint64_t dims[2] = {uint64_t(K), uint64_t(M)};
+    const uint64_t str[1] = {uint64_t(lda)};
+    const uint32_t box[2] = {uint32_t(kBK), uint32_t(kBM)};
+    if (encode_u8(&tA, A, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return W4A8_ERR_TENSORMAP;
+  }
+  {
+    const uint64_t dims[2] = {uint64_t(K / 2), uint64_t(N)};
+    const uint64_t str[1] = {uint64_t(ldw)};
+    const uint32_t box[2] = {uint32_t(kBK / 2), uint32_t(bnl)};
+    if (encode_u8(&tW, W, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)) return W4A8_ERR_TENSORMAP;
+  }
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int grid = cta == 2 ? 2 * std::min(tiles, slots) : std::min(tiles, sms);
+  return launch_w4(bn, cta, tA, tW, p, grid, stream);
+}
+
 }  // namespace
 }  // namespace w4a8
 
@@ -133,6 +258,7 @@ extern "C" int w4a8_gemm(const int8_t* A, int64_t lda, const void* W, int64_t ld
   const int tiles_m = (M + kBM - 1) / kBM;
   int bn = N > 128 ? 256 : (N > 64 ? 128 : 64);
   while (bn > 64 && tiles_m * ((N + bn - 1) / bn) < sms) bn >>= 1;
+  if (i4) return gemm_w4(A, lda, W, ldw, M, N, K, epi, C, ldc, bn, sms, static_cast<cudaStream_t>(stream));
 
   KParams p;
   std::memset(&p, 0, sizeof(p));

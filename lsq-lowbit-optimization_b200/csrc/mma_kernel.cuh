@@ -113,6 +113,7 @@ struct KParams {
   uint32_t a_off, b_off, bp_off, h_off;  // smem region offsets (from 1024-aligned base)
   uint32_t a_stage_bytes, b_stage_bytes, bp_stage_bytes;
   uint32_t tx_bytes;  // TMA bytes per operand stage
+  int pk_stages, b8_stages;  // W4 GEMM: packed-weight and int8-weight ring depths
   int b_resident;     // conv, one n-tile: all weight k-blocks stay in smem
   uint32_t bres_tx_bytes;
   uint32_t tmem_cols;

@@ -115,6 +115,24 @@ def test_linear_op_matches_oracle(cuda):
         assert_close(got, want.astype(np.float32), 1e-3, "linear tolerance")
 
 
+def test_gemm_cta_pair_ragged(cuda):
+    """Large W4 GEMMs run on CTA pairs (256 x 256 tiles, each CTA holding
+    half of B); ragged M, N and K exercise the follower's partial rows, a
+    partial n-tile and a partial k-block. Rows sampled from every 128-row
+    block (both CTAs of each pair) are checked bit-exact."""
+    m, n, k = 2300, 2100, 1056
+    gen = torch.Generator().manual_seed(2300)
+    a = torch.randint(-128, 128, (m, k), dtype=torch.int8, generator=gen)
+    w = torch.randint(-8, 8, (n, k), dtype=torch.int8, generator=gen)
+    bp = orc.pack_int4(w.numpy())
+    got = ext.int4_int8_gemm(a.to(cuda), to_dev(bp, cuda)).cpu().numpy()
+    rows = np.unique(np.concatenate([np.arange(0, m, 128), np.arange(127, m, 128), np.arange(61, m, 128),
+                                     [m - 1]]))
+    want = orc.gemm_s32(a.numpy()[rows], w.numpy())
+    assert np.array_equal(got[rows], want)
+    assert ext.device_error() == 0
+
+
 @pytest.mark.parametrize("m", [1, 32, 256, 4096])
 @pytest.mark.parametrize("nk", [1024, 4096, 8192])
 def test_gemm_sweep_sampled_bitexact(cuda, m, nk):
