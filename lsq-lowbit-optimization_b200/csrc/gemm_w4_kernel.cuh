@@ -61,6 +61,16 @@ __device__ __forceinline__ bool warp_wait_all(int lane, volatile int* abort_flag
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
+// Position in a ring of `n` stages: stage index and phase parity, advanced
+// by `step` (< n + 1) per k-block without division.
+struct RingPos {
+  uint32_t s = 0, ph = 0;
+  __device__ __forceinline__ void advance(uint32_t step, uint32_t n) {
+    s += step;
+    if (s >= n) { s -= n; ph ^= 1; }
+  }
+};
+
 // Wait until the last fill of every stage of a ring has landed (no TMA may
 // still be writing shared memory when the CTA exits). `q` fills were issued.
 __device__ __forceinline__ void drain_ring(uint64_t* full, int stages, uint32_t q, volatile int* abort_flag) {
@@ -151,16 +161,17 @@ __global__ void __launch_bounds__(kW4Threads, 1)
       uint8_t* ring = base + (is_a ? p.a_off : p.bp_off);
       const uint32_t stage_bytes = is_a ? uint32_t(kBM * kBK) : kPkBytes;
       uint32_t q = 0;
+      RingPos r;
       bool ok = true;
       for (int t = tile0; ok && t < total_tiles; t += tstep) {
         const int mt = t / p.tiles_n;
         const int nt = t - mt * p.tiles_n;
         const int row = is_a ? (kPair ? 2 * mt + int(rank) : mt) * kBM : nt * BN + int(rank) * kBNL;
-        for (int kb = 0; kb < p.num_kb; ++kb, ++q) {
-          const uint32_t s = q % S;
-          if (!mbar_wait(&empty[s], ((q / S) & 1) ^ 1, &abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[s], stage_bytes);
-          tma_load_2d(ring + s * stage_bytes, is_a ? &tmA : &tmW, &full[s], is_a ? kb * kBK : kb * (kBK / 2), row);
+        for (int kb = 0; kb < p.num_kb; ++kb, ++q, r.advance(1, S)) {
+          if (!mbar_wait(&empty[r.s], r.ph ^ 1, &abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[r.s], stage_bytes);
+          tma_load_2d(ring + r.s * stage_bytes, is_a ? &tmA : &tmW, &full[r.s], is_a ? kb * kBK : kb * (kBK / 2),
+                      row);
         }
       }
       drain_ring(full, int(S), q, &abort_flag);
@@ -173,7 +184,7 @@ __global__ void __launch_bounds__(kW4Threads, 1)
       const uint64_t tmpl = make_smem_desc(0, 16, 1024, kLayoutSw128);
       const uint32_t a0 = (base_u32 + p.a_off) >> 4, b0 = (base_u32 + p.b_off) >> 4;
       constexpr uint32_t a_step = (kBM * kBK) >> 4, b_step = kB8Bytes >> 4;
-      uint32_t q = 0;
+      RingPos ra, rb;
       int it = 0;
       bool ok = true;
       for (int t = tile0; ok && t < total_tiles; t += tstep, ++it) {
@@ -183,10 +194,10 @@ __global__ void __launch_bounds__(kW4Threads, 1)
         const uint32_t d_tmem = tmem_base + buf * BN;
         // No exits inside: a failed wait clears `ok` (later waits give up
         // within a few hundred polls) and the tile loop stops.
-        for (int kb = 0; kb < p.num_kb; ++kb, ++q) {
-          const uint32_t sa = q % Sa, sb = q % Sb;
+        for (int kb = 0; kb < p.num_kb; ++kb, ra.advance(1, Sa), rb.advance(1, Sb)) {
+          const uint32_t sa = ra.s, sb = rb.s;
           // ready_b: this k-block's weights are expanded and its A landed, in both CTAs of a pair.
-          ok &= mbar_wait(&ready_b[sb], (q / Sb) & 1, &abort_flag);
+          ok &= mbar_wait(&ready_b[sb], rb.ph, &abort_flag);
           tc_fence_after();
           const uint64_t ad = tmpl + (a0 + sa * a_step), bd = tmpl + (b0 + sb * b_step);
 #pragma unroll
@@ -273,14 +284,19 @@ __global__ void __launch_bounds__(kW4Threads, 1)
     const int gt = (u % W4Roles::kGroupWarps) * 32 + lane;
     const uint32_t src0 = uint32_t(gt) * 8;
     const uint32_t dst0 = uint32_t(gt >> 3) * 128 + (uint32_t((gt & 7) ^ ((gt >> 3) & 7)) << 4);
-    uint32_t q = 0;
+    // This group's k-blocks are q = g, g + 2, ...: ring positions start at g
+    // and advance by 2 (every ring has at least two stages).
+    const uint32_t my_tiles = tile0 < total_tiles ? uint32_t((total_tiles - tile0 + tstep - 1) / tstep) : 0u;
+    const uint32_t total_q = my_tiles * uint32_t(p.num_kb);
+    RingPos ra, rp, rb;
+    ra.advance(g, Sa);
+    rp.advance(g, Sp);
+    rb.advance(g, Sb);
     bool ok = true;
-    for (int t = tile0; ok && t < total_tiles; t += tstep) {
-      for (int kb = 0; kb < p.num_kb; ++kb, ++q) {
-        if ((q & 1) != g) continue;
-        const uint32_t sa = q % Sa, sp = q % Sp, sb = q % Sb;
-        if (!warp_wait_all(lane, &abort_flag, &full_p[sp], (q / Sp) & 1, &empty_b[sb], ((q / Sb) & 1) ^ 1,
-                           &full_a[sa], (q / Sa) & 1)) {
+    for (uint32_t q = g; q < total_q; q += 2, ra.advance(2, Sa), rp.advance(2, Sp), rb.advance(2, Sb)) {
+      {
+        const uint32_t sa = ra.s, sp = rp.s, sb = rb.s;
+        if (!warp_wait_all(lane, &abort_flag, &full_p[sp], rp.ph, &empty_b[sb], rb.ph ^ 1, &full_a[sa], ra.ph)) {
           ok = false;
           break;
         }
