@@ -16,6 +16,7 @@
 #ifndef W4A8_H_
 #define W4A8_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -99,6 +100,25 @@ typedef struct {
  */
 W4A8_API int w4a8_gemm(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int w_kind, int M, int N, int K,
               const w4a8_epilogue* epi, void* C, int64_t ldc, void* stream);
+
+/*
+ * Split-K form of w4a8_gemm for INT4 weights whose output tiles alone cannot
+ * fill the GPU (small M: decode-style linear layers). The k-blocks are split
+ * into ranges whose int32 partial sums are added (exactly) into `workspace`
+ * (int32 [M, N], zeroed by the call), then the epilogue runs over the sums.
+ * Results are identical to w4a8_gemm. workspace_bytes must be at least what
+ * w4a8_gemm_splitk_workspace reports; with a null workspace, INT8 weights
+ * or a shape that needs no split this is w4a8_gemm. Calls sharing one
+ * workspace must be ordered (one stream).
+ * Extends the reference's int4_int8_gemm path (csrc/int4_int8_kernels.cu:257-291),
+ * which has no split-K.
+ */
+W4A8_API int w4a8_gemm_splitk(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int w_kind, int M, int N,
+                              int K, const w4a8_epilogue* epi, void* C, int64_t ldc, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+/* Workspace bytes w4a8_gemm_splitk needs for this shape (0: no split). */
+W4A8_API int w4a8_gemm_splitk_workspace(int M, int N, int K, int w_kind, size_t* bytes);
 
 /* Convolution geometry. Input is int8 NHWC [n, h, w, c] with c in
  * {16, 32, 64} or c a multiple of 128 (pad channels with zero codes and

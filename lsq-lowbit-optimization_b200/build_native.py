@@ -17,7 +17,7 @@ CSRC = HERE / "csrc"
 INCLUDE = HERE.parent / "include"
 LIB = HERE / "libw4a8.so"
 SOURCES = ["gemm_conv.cu", "aux_kernels.cu"]
-HEADERS = ["ptx.cuh", "mma_kernel.cuh", "gemm_w4_kernel.cuh", "tensormap.cuh"]
+HEADERS = ["ptx.cuh", "mma_kernel.cuh", "gemm_w4_kernel.cuh", "gemv_w4.cuh", "tensormap.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -3,6 +3,7 @@
 #include <algorithm>
 
 #include "gemm_w4_kernel.cuh"
+#include "gemv_w4.cuh"
 #include "mma_kernel.cuh"
 #include "tensormap.cuh"
 
@@ -42,9 +43,9 @@ int launch_t(const CUtensorMap& tA, const CUtensorMap& tW, const CUtensorMap* tH
   return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH;
 }
 
-template <int BN, int CTA>
+template <int BN, int CTA, bool SWAP>
 int launch_w4_t(const CUtensorMap& tA, const CUtensorMap& tW, const KParams& p, int grid, cudaStream_t st) {
-  auto kern = w4a8_gemm_w4_kernel<BN, CTA>;
+  auto kern = w4a8_gemm_w4_kernel<BN, CTA, SWAP>;
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -75,13 +76,21 @@ int launch_w4_t(const CUtensorMap& tA, const CUtensorMap& tW, const KParams& p, 
   return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH;
 }
 
-int launch_w4(int bn, int cta, const CUtensorMap& tA, const CUtensorMap& tW, const KParams& p, int grid,
+int launch_w4(int bn, int cta, bool swap, const CUtensorMap& tA, const CUtensorMap& tW, const KParams& p, int grid,
               cudaStream_t st) {
-  if (cta == 2) return launch_w4_t<256, 2>(tA, tW, p, grid, st);
+  if (cta == 2) return launch_w4_t<256, 2, false>(tA, tW, p, grid, st);
+  if (swap) {
+    switch (bn) {
+      case 32: return launch_w4_t<32, 1, true>(tA, tW, p, grid, st);
+      case 64: return launch_w4_t<64, 1, true>(tA, tW, p, grid, st);
+      case 128: return launch_w4_t<128, 1, true>(tA, tW, p, grid, st);
+      default: return W4A8_ERR_UNSUPPORTED;
+    }
+  }
   switch (bn) {
-    case 64: return launch_w4_t<64, 1>(tA, tW, p, grid, st);
-    case 128: return launch_w4_t<128, 1>(tA, tW, p, grid, st);
-    case 256: return launch_w4_t<256, 1>(tA, tW, p, grid, st);
+    case 64: return launch_w4_t<64, 1, false>(tA, tW, p, grid, st);
+    case 128: return launch_w4_t<128, 1, false>(tA, tW, p, grid, st);
+    case 256: return launch_w4_t<256, 1, false>(tA, tW, p, grid, st);
     default: return W4A8_ERR_UNSUPPORTED;
   }
 }
@@ -96,7 +105,7 @@ int pair_slots() {
   std::memset(&dummy, 0, sizeof(dummy));
   KParams p;
   std::memset(&p, 0, sizeof(p));
-  const int n = launch_w4(256, 2, dummy, dummy, p, -1, nullptr);
+  const int n = launch_w4(256, 2, false, dummy, dummy, p, -1, nullptr);
   if (n > 0 && dev >= 0 && dev < 64) cached[dev] = n;
   return n > 0 ? n : 0;
 }
@@ -154,27 +163,89 @@ int pick_stages(uint32_t per_stage, uint32_t reserved) {
 
 int floordiv(int a, int b) { return a >= 0 ? a / b : -((-a + b - 1) / b); }
 
+// A few tokens (M <= 8, K a multiple of 64, activations fit in shared
+// memory) run on the CUDA-core GEMV, which streams the packed weights
+// straight into registers.
+bool use_gemv(int M, int K) {
+  return M >= 1 && M <= kGemvMaxTokens && K % 64 == 0 && gemv_smem_bytes(kGemvMaxTokens, K) <= 200 * 1024;
+}
+
+template <int MT>
+int launch_gemv_t(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K,
+                  const EpiParams& e, cudaStream_t st) {
+  auto kern = w4a8_gemv_w4_kernel<MT>;
+  const size_t smem = gemv_smem_bytes(MT, K);
+  if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+    return W4A8_ERR_LAUNCH;
+  kern<<<unsigned((N + 31) / 32), kGemvWarps * 32, smem, st>>>(A, lda, static_cast<const uint8_t*>(W), ldw, M, N, K, e);
+  return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH;
+}
+
+int gemv_w4(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K,
+            const w4a8_epilogue* epi, void* C, int64_t ldc, cudaStream_t st) {
+  EpiParams e;
+  std::memset(&e, 0, sizeof(e));
+  fill_epi(e, epi, C, N);
+  e.acc_fits_22 = (double)K * 128.0 * 8.0 < 4194304.0;
+  e.s_img = 0;
+  e.s_pix = ldc;
+  e.s_ch = 1;
+  if (M <= 1) return launch_gemv_t<1>(A, lda, W, ldw, M, N, K, e, st);
+  if (M <= 2) return launch_gemv_t<2>(A, lda, W, ldw, M, N, K, e, st);
+  if (M <= 4) return launch_gemv_t<4>(A, lda, W, ldw, M, N, K, e, st);
+  return launch_gemv_t<8>(A, lda, W, ldw, M, N, K, e, st);
+}
+
+// Split-K plan for a small-M (<= 128) W4 GEMM whose output tiles alone
+// cannot fill the GPU. Tiles are 128 channels x bn tokens (bn = 32, 64 or
+// 128 covering M, swapped operands); about four work units per SM, each at
+// least two k-blocks long. Returns the number of splits (0: no split).
+int splitk_plan(int M, int N, int K, int sms, int& bn, int& kb_per) {
+  const int num_kb = (K + kBK - 1) / kBK;
+  if (M > 64 || num_kb < 16 || use_gemv(M, K)) return 0;
+  bn = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
+  const int tiles = (N + kBM - 1) / kBM;
+  if (tiles >= sms || num_kb < 4) return 0;
+  int s = std::max(1, std::min(4 * sms / tiles, num_kb / 2));
+  kb_per = (num_kb + s - 1) / s;
+  s = (num_kb + kb_per - 1) / kb_per;
+  return s > 1 ? s : 0;
+}
+
 // W4 GEMM on the three-ring kernel; CTA pairs (256 x 256 tiles) when there
-// are enough of them to fill the GPU.
+// are enough of them to fill the GPU; split-K into `ws` (int32 [M, N],
+// ws_bytes) when a workspace is given and the tiles are too few.
 int gemm_w4(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K,
-            const w4a8_epilogue* epi, void* C, int64_t ldc, int bn, int sms, cudaStream_t stream) {
+            const w4a8_epilogue* epi, void* C, int64_t ldc, int bn, int sms, int* ws, size_t ws_bytes,
+            cudaStream_t stream) {
+  if (use_gemv(M, K)) return gemv_w4(A, lda, W, ldw, M, N, K, epi, C, ldc, stream);
+  int kb_per = 0, bn_split = bn;
+  const int splits = ws ? splitk_plan(M, N, K, sms, bn_split, kb_per) : 0;
+  if (splits && ws_bytes < size_t(M) * size_t(N) * 4) return W4A8_ERR_ARG;
   const int pair_tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * ((N + 255) / 256);
-  const int slots = (N >= 256 && M > kBM && pair_tiles >= sms / 2) ? pair_slots() : 0;
+  const int slots = (!splits && N >= 256 && M > kBM && pair_tiles >= sms / 2) ? pair_slots() : 0;
   const int cta = slots > 0 ? 2 : 1;
   if (cta == 2) bn = 256;
-  const int bnl = bn / cta;
+  const bool swap = splits > 0;  // split-K runs with swapped operands (see splitk_plan)
+  if (swap) bn = bn_split;
+  const int bnl = swap ? kBM : bn / cta;  // weight rows per CTA
+  const int xrows = swap ? bn : kBM;      // activation rows per stage
 
   KParams p;
   std::memset(&p, 0, sizeof(p));
   p.M = M;
   p.N = N;
   p.num_kb = (K + kBK - 1) / kBK;
-  p.tiles_m = cta == 2 ? (M + 2 * kBM - 1) / (2 * kBM) : (M + kBM - 1) / kBM;
-  p.tiles_n = (N + bn - 1) / bn;
+  p.tiles_m = swap ? (M + bn - 1) / bn : (cta == 2 ? (M + 2 * kBM - 1) / (2 * kBM) : (M + kBM - 1) / kBM);
+  p.tiles_n = swap ? (N + kBM - 1) / kBM : (N + bn - 1) / bn;
+  p.k_splits = splits ? splits : 1;
+  p.kb_per_split = splits ? kb_per : p.num_kb;
+  p.ws = splits ? ws : nullptr;
+  p.ws_ld = N;
   // Ring depths: four packed stages (weight bytes arrive far ahead of use),
   // then A and int8 B stages added in step (A first) while they fit; the
   // int8 ring covers MMA completion -> unpack -> proxy fence -> arrive.
-  const int64_t a_bytes = kBM * kBK, pk_bytes = int64_t(bnl) * (kBK / 2), b8_bytes = int64_t(bnl) * kBK;
+  const int64_t a_bytes = int64_t(xrows) * kBK, pk_bytes = int64_t(bnl) * (kBK / 2), b8_bytes = int64_t(bnl) * kBK;
   int sa = 2, sp = 4, sb = 2;
   int64_t left = kSmemBudget - sa * a_bytes - sp * pk_bytes - sb * b8_bytes;
   if (left < 0) return W4A8_ERR_UNSUPPORTED;
@@ -205,7 +276,7 @@ int gemm_w4(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int M, int
   {
     const uint64_t dims[2] = {uint64_t(K), uint64_t(M)};
     const uint64_t str[1] = {uint64_t(lda)};
-    const uint32_t box[2] = {uint32_t(kBK), uint32_t(kBM)};
+    const uint32_t box[2] = {uint32_t(kBK), uint32_t(xrows)};
     if (encode_u8(&tA, A, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B)) return W4A8_ERR_TENSORMAP;
   }
   {
@@ -214,9 +285,14 @@ int gemm_w4(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int M, int
     const uint32_t box[2] = {uint32_t(kBK / 2), uint32_t(bnl)};
     if (encode_u8(&tW, W, 2, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE)) return W4A8_ERR_TENSORMAP;
   }
-  const int tiles = p.tiles_m * p.tiles_n;
-  const int grid = cta == 2 ? 2 * std::min(tiles, slots) : std::min(tiles, sms);
-  return launch_w4(bn, cta, tA, tW, p, grid, stream);
+  const int units = p.tiles_m * p.tiles_n * p.k_splits;
+  const int grid = cta == 2 ? 2 * std::min(units, slots) : std::min(units, sms);
+  if (splits && cudaMemsetAsync(ws, 0, size_t(M) * size_t(N) * 4, stream) != cudaSuccess) return W4A8_ERR_LAUNCH;
+  if (int rc = launch_w4(bn, cta, swap, tA, tW, p, grid, stream)) return rc;
+  if (!splits) return W4A8_OK;
+  const long long threads = (long long)M * ((N + 15) / 16);
+  w4a8_splitk_finish_kernel<<<unsigned((threads + 255) / 256), 256, 0, stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH;
 }
 
 }  // namespace
@@ -242,23 +318,64 @@ extern "C" int w4a8_device_error(unsigned* bits) {
   return W4A8_OK;
 }
 
-extern "C" int w4a8_gemm(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int w_kind, int M, int N,
-                         int K, const w4a8_epilogue* epi, void* C, int64_t ldc, void* stream) {
+namespace {
+// Shared argument checks of the GEMM entry points; W4A8_OK + *empty when
+// there is nothing to compute.
+int check_gemm(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int w_kind, int M, int N, int K,
+               const w4a8_epilogue* epi, const void* C, int64_t ldc, bool* empty) {
+  *empty = false;
   if (M < 0 || N < 0 || K <= 0) return W4A8_ERR_ARG;
   if (w_kind != W4A8_W_INT8 && w_kind != W4A8_W_INT4) return W4A8_ERR_ARG;
   const bool i4 = w_kind == W4A8_W_INT4;
   if (i4 && (K & 1)) return W4A8_ERR_ARG;
   if (int rc = check_epilogue(epi)) return rc;
-  if (M == 0 || N == 0) return W4A8_OK;
+  if (M == 0 || N == 0) {
+    *empty = true;
+    return W4A8_OK;
+  }
   if (!A || !W || !C) return W4A8_ERR_ARG;
   if (lda < K || ldw < (i4 ? K / 2 : K) || ldc < N) return W4A8_ERR_ARG;
   if ((lda % 16) || (ldw % 16) || !aligned16(A) || !aligned16(W)) return W4A8_ERR_ALIGN;
+  return W4A8_OK;
+}
+}  // namespace
+
+extern "C" int w4a8_gemm_splitk_workspace(int M, int N, int K, int w_kind, size_t* bytes) {
+  if (!bytes || M < 0 || N < 0 || K <= 0) return W4A8_ERR_ARG;
+  int bn = 0, kb_per = 0;
+  const bool split = w_kind == W4A8_W_INT4 && M > 0 && N > 0 && splitk_plan(M, N, K, device_sms(), bn, kb_per) > 0;
+  *bytes = split ? size_t(M) * size_t(N) * 4 : 0;
+  return W4A8_OK;
+}
+
+extern "C" int w4a8_gemm_splitk(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int w_kind, int M, int N,
+                                int K, const w4a8_epilogue* epi, void* C, int64_t ldc, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  bool empty = false;
+  if (int rc = check_gemm(A, lda, W, ldw, w_kind, M, N, K, epi, C, ldc, &empty)) return rc;
+  if (empty) return W4A8_OK;
+  if (w_kind != W4A8_W_INT4 || !workspace) return w4a8_gemm(A, lda, W, ldw, w_kind, M, N, K, epi, C, ldc, stream);
+  if (!aligned16(workspace)) return W4A8_ERR_ALIGN;
+  const int sms = device_sms();
+  const int tiles_m = (M + kBM - 1) / kBM;
+  int bn = N > 128 ? 256 : (N > 64 ? 128 : 64);
+  while (bn > 64 && tiles_m * ((N + bn - 1) / bn) < sms) bn >>= 1;
+  return gemm_w4(A, lda, W, ldw, M, N, K, epi, C, ldc, bn, sms, static_cast<int*>(workspace), workspace_bytes,
+                 static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int w4a8_gemm(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int w_kind, int M, int N,
+                         int K, const w4a8_epilogue* epi, void* C, int64_t ldc, void* stream) {
+  bool empty = false;
+  if (int rc = check_gemm(A, lda, W, ldw, w_kind, M, N, K, epi, C, ldc, &empty)) return rc;
+  if (empty) return W4A8_OK;
+  const bool i4 = w_kind == W4A8_W_INT4;
 
   const int sms = device_sms();
   const int tiles_m = (M + kBM - 1) / kBM;
   int bn = N > 128 ? 256 : (N > 64 ? 128 : 64);
   while (bn > 64 && tiles_m * ((N + bn - 1) / bn) < sms) bn >>= 1;
-  if (i4) return gemm_w4(A, lda, W, ldw, M, N, K, epi, C, ldc, bn, sms, static_cast<cudaStream_t>(stream));
+  if (i4) return gemm_w4(A, lda, W, ldw, M, N, K, epi, C, ldc, bn, sms, nullptr, 0, static_cast<cudaStream_t>(stream));
 
   KParams p;
   std::memset(&p, 0, sizeof(p));

@@ -71,6 +71,22 @@ struct RingPos {
   }
 };
 
+// Work unit u of the persistent loop: output tile (mt, nt) and the k-block
+// range [kb0, kb1) of its split (one split covers all k-blocks).
+struct Unit {
+  int mt, nt, kb0, kb1;
+};
+__device__ __forceinline__ Unit unit_of(const KParams& p, int u) {
+  Unit r;
+  const int ks = u % p.k_splits;
+  const int tile = u / p.k_splits;
+  r.mt = tile / p.tiles_n;
+  r.nt = tile - r.mt * p.tiles_n;
+  r.kb0 = ks * p.kb_per_split;
+  r.kb1 = min(r.kb0 + p.kb_per_split, p.num_kb);
+  return r;
+}
+
 // Wait until the last fill of every stage of a ring has landed (no TMA may
 // still be writing shared memory when the CTA exits). `q` fills were issued.
 __device__ __forceinline__ void drain_ring(uint64_t* full, int stages, uint32_t q, volatile int* abort_flag) {
@@ -82,13 +98,18 @@ __device__ __forceinline__ void drain_ring(uint64_t* full, int stages, uint32_t 
   }
 }
 
-template <int BN, int kCta>
+// kSwap (small M, split-K only): the MMA computes C^T = W . X^T, so the 128
+// weight rows of a tile (output channels) are the MMA's M and TMEM lanes and
+// BN tokens are its N. A warp then holds 32 consecutive channels of each
+// token, and its split-K partial sums go out as 128-byte coalesced adds.
+template <int BN, int kCta, bool kSwap>
 __global__ void __launch_bounds__(kW4Threads, 1)
     w4a8_gemm_w4_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                         const __grid_constant__ KParams p) {
   constexpr bool kPair = kCta == 2;
-  static_assert(kCta == 1 || (kPair && BN == 256), "CTA pairs use 256-wide tiles");
-  constexpr int kBNL = BN / kCta;               // B rows held by this CTA
+  static_assert(kCta == 1 || (kPair && BN == 256 && !kSwap), "CTA pairs use 256-wide tiles");
+  constexpr int kBNL = kSwap ? kBM : BN / kCta;  // weight rows held by this CTA
+  constexpr int kXRows = kSwap ? BN : kBM;       // activation rows per stage
   constexpr int kNB = 2;                        // TMEM accumulator buffers
   constexpr int kSetWarps = W4Roles::kEpiWarps / kNB;
   static_assert(kSetWarps == 4, "one epilogue warp per TMEM lane quadrant and buffer");
@@ -149,7 +170,7 @@ __global__ void __launch_bounds__(kW4Threads, 1)
   if constexpr (kPair) cluster_sync();  // the peer's barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
-  const int total_tiles = p.tiles_m * p.tiles_n;
+  const int total_tiles = p.tiles_m * p.tiles_n * p.k_splits;  // work units
 
   if (warp == 0 || warp == 2) {
     // ------------------------- A / packed producers -------------------------
@@ -159,15 +180,14 @@ __global__ void __launch_bounds__(kW4Threads, 1)
       uint64_t* empty = is_a ? empty_a : empty_p;
       const uint32_t S = is_a ? Sa : Sp;
       uint8_t* ring = base + (is_a ? p.a_off : p.bp_off);
-      const uint32_t stage_bytes = is_a ? uint32_t(kBM * kBK) : kPkBytes;
+      const uint32_t stage_bytes = is_a ? uint32_t(kXRows * kBK) : kPkBytes;
       uint32_t q = 0;
       RingPos r;
       bool ok = true;
       for (int t = tile0; ok && t < total_tiles; t += tstep) {
-        const int mt = t / p.tiles_n;
-        const int nt = t - mt * p.tiles_n;
-        const int row = is_a ? (kPair ? 2 * mt + int(rank) : mt) * kBM : nt * BN + int(rank) * kBNL;
-        for (int kb = 0; kb < p.num_kb; ++kb, ++q, r.advance(1, S)) {
+        const Unit un = unit_of(p, t);
+        const int row = is_a ? (kPair ? 2 * un.mt + int(rank) : un.mt) * kXRows : un.nt * (kSwap ? kBM : BN) + int(rank) * kBNL;
+        for (int kb = un.kb0; kb < un.kb1; ++kb, ++q, r.advance(1, S)) {
           if (!mbar_wait(&empty[r.s], r.ph ^ 1, &abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[r.s], stage_bytes);
           tma_load_2d(ring + r.s * stage_bytes, is_a ? &tmA : &tmW, &full[r.s], is_a ? kb * kBK : kb * (kBK / 2),
@@ -180,10 +200,10 @@ __global__ void __launch_bounds__(kW4Threads, 1)
   } else if (warp == 1) {
     // ------------------------------- MMA ------------------------------------
     if (lane == 0 && rank == 0) {  // in a CTA pair the leader issues for both
-      constexpr uint32_t idesc = make_idesc_i8(kCta * kBM, BN);
+      constexpr uint32_t idesc = make_idesc_i8(kCta * kBM, BN);  // swap: M = 128 channels, N = BN tokens
       const uint64_t tmpl = make_smem_desc(0, 16, 1024, kLayoutSw128);
       const uint32_t a0 = (base_u32 + p.a_off) >> 4, b0 = (base_u32 + p.b_off) >> 4;
-      constexpr uint32_t a_step = (kBM * kBK) >> 4, b_step = kB8Bytes >> 4;
+      constexpr uint32_t a_step = (kXRows * kBK) >> 4, b_step = kB8Bytes >> 4;
       RingPos ra, rb;
       int it = 0;
       bool ok = true;
@@ -194,18 +214,20 @@ __global__ void __launch_bounds__(kW4Threads, 1)
         const uint32_t d_tmem = tmem_base + buf * BN;
         // No exits inside: a failed wait clears `ok` (later waits give up
         // within a few hundred polls) and the tile loop stops.
-        for (int kb = 0; kb < p.num_kb; ++kb, ra.advance(1, Sa), rb.advance(1, Sb)) {
+        const Unit un = unit_of(p, t);
+        for (int kb = un.kb0; kb < un.kb1; ++kb, ra.advance(1, Sa), rb.advance(1, Sb)) {
           const uint32_t sa = ra.s, sb = rb.s;
           // ready_b: this k-block's weights are expanded and its A landed, in both CTAs of a pair.
           ok &= mbar_wait(&ready_b[sb], rb.ph, &abort_flag);
           tc_fence_after();
-          const uint64_t ad = tmpl + (a0 + sa * a_step), bd = tmpl + (b0 + sb * b_step);
+          const uint64_t xd = tmpl + (a0 + sa * a_step), wd = tmpl + (b0 + sb * b_step);
+          const uint64_t ad = kSwap ? wd : xd, bd = kSwap ? xd : wd;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             if constexpr (kPair)
-              mma_i8_ss_pair(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kb | j) != 0 ? 1u : 0u);
+              mma_i8_ss_pair(d_tmem, ad + 2 * j, bd + 2 * j, idesc, ((kb - un.kb0) | j) != 0 ? 1u : 0u);
             else
-              mma_i8_ss(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kb | j) != 0 ? 1u : 0u);
+              mma_i8_ss(d_tmem, ad + 2 * j, bd + 2 * j, idesc, ((kb - un.kb0) | j) != 0 ? 1u : 0u);
           }
           if constexpr (kPair) {
             mma_commit_pair_both(&empty_a[sa]);
@@ -250,19 +272,36 @@ __global__ void __launch_bounds__(kW4Threads, 1)
         break;
       }
       tc_fence_after();
-      const int mt = t / p.tiles_n;
-      const int nt = t - mt * p.tiles_n;
+      const Unit un = unit_of(p, t);
       long long out_off = 0, prow = 0;
-      const bool valid = row_coords<false>(p, kPair ? 2 * mt + int(rank) : mt, m, out_off, prow);
+      const bool valid = !kSwap && row_coords<false>(p, kPair ? 2 * un.mt + int(rank) : un.mt, m, out_off, prow);
       const uint32_t t_addr = tmem_base + (uint32_t(q4 * 32) << 16) + set * BN;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         uint32_t acc[16];
         tmem_ld16(t_addr + c0, acc);
         tmem_ld_wait();
-        if (valid) {
-          const int n = nt * BN + c0;
-          epilogue16(p.epi, k, acc, n, out_off + (long long)n * p.epi.s_ch, prow);
+        if constexpr (kSwap) {
+          // Lane = channel, columns = tokens: C[token][channel] += acc.
+          const int ch = un.nt * kBM + m, tok0 = un.mt * BN + c0;
+          if (ch < p.N) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (tok0 + i < p.M) atomicAdd(p.ws + (long long)(tok0 + i) * p.ws_ld + ch, int(acc[i]));
+          }
+        } else if (valid) {
+          const int n = un.nt * BN + c0;
+          if (p.k_splits > 1) {
+            // Split-K: add this k-range's partial sums (int32 addition is
+            // exact in any order); the finish kernel applies the epilogue.
+            int* dst = p.ws + prow * p.ws_ld + n;
+            const int nc = min(16, p.N - n);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (i < nc) atomicAdd(dst + i, int(acc[i]));
+          } else {
+            epilogue16(p.epi, k, acc, n, out_off + (long long)n * p.epi.s_ch, prow);
+          }
         }
       }
       tc_fence_before();
@@ -284,17 +323,15 @@ __global__ void __launch_bounds__(kW4Threads, 1)
     const int gt = (u % W4Roles::kGroupWarps) * 32 + lane;
     const uint32_t src0 = uint32_t(gt) * 8;
     const uint32_t dst0 = uint32_t(gt >> 3) * 128 + (uint32_t((gt & 7) ^ ((gt >> 3) & 7)) << 4);
-    // This group's k-blocks are q = g, g + 2, ...: ring positions start at g
-    // and advance by 2 (every ring has at least two stages).
-    const uint32_t my_tiles = tile0 < total_tiles ? uint32_t((total_tiles - tile0 + tstep - 1) / tstep) : 0u;
-    const uint32_t total_q = my_tiles * uint32_t(p.num_kb);
+    // This group's k-blocks are q = g, g + 2, ... of the CTA's sequence; the
+    // ring positions advance with every k-block.
     RingPos ra, rp, rb;
-    ra.advance(g, Sa);
-    rp.advance(g, Sp);
-    rb.advance(g, Sb);
+    uint32_t q = 0;
     bool ok = true;
-    for (uint32_t q = g; q < total_q; q += 2, ra.advance(2, Sa), rp.advance(2, Sp), rb.advance(2, Sb)) {
-      {
+    for (int t = tile0; ok && t < total_tiles; t += tstep) {
+      const Unit un = unit_of(p, t);
+      for (int kb = un.kb0; kb < un.kb1; ++kb, ++q, ra.advance(1, Sa), rp.advance(1, Sp), rb.advance(1, Sb)) {
+        if ((q & 1) != g) continue;
         const uint32_t sa = ra.s, sp = rp.s, sb = rb.s;
         if (!warp_wait_all(lane, &abort_flag, &full_p[sp], rp.ph, &empty_b[sb], rb.ph ^ 1, &full_a[sa], ra.ph)) {
           ok = false;
@@ -338,6 +375,37 @@ __global__ void __launch_bounds__(kW4Threads, 1)
     else
       tmem_dealloc(tmem_base, kTmemCols);
   }
+}
+
+// Split-K finish: the fused epilogue over the int32 sums; one thread per
+// (row, 16 columns).
+__global__ void __launch_bounds__(256) w4a8_splitk_finish_kernel(const __grid_constant__ KParams p) {
+  const int chunks = (p.N + 15) / 16;
+  const long long idx = blockIdx.x * 256LL + threadIdx.x;
+  if (idx >= (long long)p.M * chunks) return;
+  const int row = int(idx / chunks);
+  const int n = int(idx - (long long)row * chunks) * 16;
+  EpiConsts k;
+  k.rs = p.epi.out_kind == 3 ? __frcp_rn(p.epi.out_scale) : 1.0f;
+  k.qnf = float(p.epi.qn);
+  k.qpf = float(p.epi.qp);
+  k.relu_in_clamp = p.epi.out_kind == 3 && p.epi.qn >= 0 && p.epi.aux == nullptr;
+  const int* src = p.ws + row * p.ws_ld + n;
+  uint32_t acc[16];
+  if (n + 16 <= p.N && (p.ws_ld & 3) == 0) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int4 v = *reinterpret_cast<const int4*>(src + 4 * g);
+      acc[4 * g] = uint32_t(v.x);
+      acc[4 * g + 1] = uint32_t(v.y);
+      acc[4 * g + 2] = uint32_t(v.z);
+      acc[4 * g + 3] = uint32_t(v.w);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] = n + i < p.N ? uint32_t(src[i]) : 0u;
+  }
+  epilogue16(p.epi, k, acc, n, (long long)row * p.epi.s_pix + (long long)n * p.epi.s_ch, row);
 }
 
 }  // namespace w4a8

@@ -114,6 +114,9 @@ struct KParams {
   uint32_t a_stage_bytes, b_stage_bytes, bp_stage_bytes;
   uint32_t tx_bytes;  // TMA bytes per operand stage
   int pk_stages, b8_stages;  // W4 GEMM: packed-weight and int8-weight ring depths
+  int k_splits, kb_per_split;  // W4 GEMM split-K: units are (tile, k-range)
+  int* ws;                     // split-K: int32 partial sums, [M, ws_ld], zeroed before the launch
+  long long ws_ld;
   int b_resident;     // conv, one n-tile: all weight k-blocks stay in smem
   uint32_t bres_tx_bytes;
   uint32_t tmem_cols;

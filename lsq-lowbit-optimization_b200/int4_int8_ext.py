@@ -77,6 +77,9 @@ class ConvGeom(ctypes.Structure):
 _vp, _i64, _int, _f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float
 _SIGNATURES = {
     "w4a8_gemm": [_vp, _i64, _vp, _i64, _int, _int, _int, _int, ctypes.POINTER(Epilogue), _vp, _i64, _vp],
+    "w4a8_gemm_splitk": [_vp, _i64, _vp, _i64, _int, _int, _int, _int, ctypes.POINTER(Epilogue), _vp, _i64, _vp,
+                         ctypes.c_size_t, _vp],
+    "w4a8_gemm_splitk_workspace": [_int, _int, _int, _int, ctypes.POINTER(ctypes.c_size_t)],
     "w4a8_conv2d": [_vp, _vp, _int, _i64, ctypes.POINTER(ConvGeom), ctypes.POINTER(Epilogue), _vp, _vp],
     "w4a8_quantize_rows": [_vp, _i64, _vp, _i64, _i64, _int, _f32, _int, _int, _vp],
     "w4a8_quantize_nchw_to_nhwc": [_vp, _vp, _int, _int, _int, _int, _int, _f32, _int, _int, _vp],
@@ -168,10 +171,34 @@ def gemm(a: torch.Tensor, w: torch.Tensor, w_kind: int, k: int, epi: Epilogue, o
     must be multiples of 16. ``out`` is row-major with its own row stride."""
     m, n = a.shape[0], w.shape[0]
     with torch.cuda.device(a.device):
+        ws_bytes = splitk_workspace_bytes(m, n, k, w_kind)
+        if ws_bytes:
+            # Small-M INT4 GEMM: split-K into an int32 workspace from torch's
+            # stream-ordered allocator (released back to it after this call).
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=a.device)
+            rc = lib().w4a8_gemm_splitk(a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), w_kind, m, n, k,
+                                        ctypes.byref(epi), out.data_ptr(), out.stride(0), ws.data_ptr(), ws_bytes,
+                                        _stream(a))
+            _check(rc, "w4a8_gemm_splitk")
+            return out
         rc = lib().w4a8_gemm(a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), w_kind, m, n, k,
                              ctypes.byref(epi), out.data_ptr(), out.stride(0), _stream(a))
     _check(rc, "w4a8_gemm")
     return out
+
+
+_ws_cache: dict = {}
+
+
+def splitk_workspace_bytes(m: int, n: int, k: int, w_kind: int) -> int:
+    """Workspace bytes of the split-K GEMM for this shape on the current
+    device (0 when the shape runs unsplit)."""
+    key = (torch.cuda.current_device(), m, n, k, w_kind)
+    if key not in _ws_cache:
+        nbytes = ctypes.c_size_t(0)
+        _check(lib().w4a8_gemm_splitk_workspace(m, n, k, w_kind, ctypes.byref(nbytes)), "w4a8_gemm_splitk_workspace")
+        _ws_cache[key] = int(nbytes.value)
+    return _ws_cache[key]
 
 
 def conv2d_nhwc(x: torch.Tensor, w: torch.Tensor, w_kind: int, geom: ConvGeom, epi: Epilogue,

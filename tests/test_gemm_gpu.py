@@ -5,6 +5,8 @@ check, benchmarks/benchmark_inference.py:62-79). Float epilogues follow the
 documented float32 op order and are compared bit-exact as well; the
 contract tolerance for them is rel 1e-3.
 """
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -113,6 +115,46 @@ def test_linear_op_matches_oracle(cuda):
         want = orc.linear(x, bp, 0.05, 0.0123, -127, 127, bias, half)
         assert_equal(got, want, f"linear half={half}")
         assert_close(got, want.astype(np.float32), 1e-3, "linear tolerance")
+
+
+@pytest.mark.parametrize("m", [1, 5, 37])
+def test_gemm_small_m_paths(cuda, m):
+    """Small-M INT4 GEMMs: up to 8 tokens run on the CUDA-core GEMV (packed
+    weights streamed into registers), 9..64 tokens split K across work units
+    (int32 partial sums in a workspace, epilogue after the sum). The fused
+    float epilogue with residual, ReLU and float side output, and the int8
+    requantisation, must equal the oracle and the workspace-free entry point
+    bit for bit."""
+    g = rng(900 + m)
+    n, k = 1000, 2048
+    x = rand_i8(g, (m, k))
+    w = rand_i4(g, (n, k))
+    alpha = g.uniform(1e-5, 1e-4, n).astype(np.float32)
+    beta = g.normal(0, 0.1, n).astype(np.float32)
+    res = g.normal(0, 1.0, (m, n)).astype(np.float32)
+    bp = orc.pack_int4(w)
+    assert ext.splitk_workspace_bytes(m, n, k, ext.W_INT4) == (0 if m <= 8 else m * n * 4)
+    y = orc.epilogue(orc.int4_int8_gemm(x, bp), alpha, beta, res, relu=True)
+    outs = {}
+    for split in (True, False):
+        out = torch.empty((m, n), dtype=torch.int8, device=cuda)
+        aux = torch.empty((m, n), dtype=torch.float32, device=cuda)
+        epi = ext.make_epilogue(ext.OUT_S8, alpha=to_dev(alpha, cuda), beta=to_dev(beta, cuda),
+                                residual=to_dev(res, cuda), res_ld=n, relu=True, out_scale=0.05, qn=0, qp=127,
+                                aux=aux, aux_ld=n)
+        xd, wd = to_dev(x, cuda), to_dev(bp, cuda)
+        if split:
+            ext.gemm(xd, wd, ext.W_INT4, k, epi, out)
+        else:
+            ext._check(ext.lib().w4a8_gemm(xd.data_ptr(), xd.stride(0), wd.data_ptr(), wd.stride(0), ext.W_INT4, m,
+                                           n, k, ctypes.byref(epi), out.data_ptr(), out.stride(0),
+                                           torch.cuda.current_stream().cuda_stream), "w4a8_gemm")
+        torch.cuda.synchronize()
+        assert_equal(aux, y, f"aux split={split}")
+        assert_equal(out, orc.quantize(y, 0.05, 0, 127), f"requant split={split}")
+        outs[split] = out
+    assert torch.equal(outs[True], outs[False])
+    assert ext.device_error() == 0
 
 
 def test_gemm_cta_pair_ragged(cuda):
