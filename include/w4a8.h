@@ -120,6 +120,22 @@ W4A8_API int w4a8_gemm_splitk(const int8_t* A, int64_t lda, const void* W, int64
 /* Workspace bytes w4a8_gemm_splitk needs for this shape (0: no split). */
 W4A8_API int w4a8_gemm_splitk_workspace(int M, int N, int K, int w_kind, size_t* bytes);
 
+/*
+ * w4a8_gemm_splitk without a workspace argument and without allocating:
+ * the int32 partial sums live in a fixed device array of
+ * W4A8_NOALLOC_SCRATCH_BYTES inside the library (located once per device,
+ * cleared by every call). INT4 weights only; shapes with M * N * 4 above
+ * W4A8_NOALLOC_SCRATCH_BYTES are rejected with W4A8_ERR_ARG. Results equal
+ * w4a8_gemm. All calls on a device share the one array, so calls that
+ * overlap in time (different streams, or host threads) race and corrupt
+ * each other's results: order them on one stream.
+ * No counterpart in the reference (its int4_int8_gemm path,
+ * csrc/int4_int8_kernels.cu:257-291, has neither split-K nor a workspace).
+ */
+#define W4A8_NOALLOC_SCRATCH_BYTES (4u << 20)
+W4A8_API int w4a8_gemm_splitk_noalloc(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int w_kind, int M,
+                                      int N, int K, const w4a8_epilogue* epi, void* C, int64_t ldc, void* stream);
+
 /* Convolution geometry. Input is int8 NHWC [n, h, w, c] with c in
  * {16, 32, 64} or c a multiple of 128 (pad channels with zero codes and
  * zero weights otherwise); c == 16 only at stride 1.

@@ -364,6 +364,44 @@ extern "C" int w4a8_gemm_splitk(const int8_t* A, int64_t lda, const void* W, int
                  static_cast<cudaStream_t>(stream));
 }
 
+namespace {
+// Scratch of w4a8_gemm_splitk_noalloc: the split-K int32 partial sums live in
+// this fixed device array instead of a caller or allocator workspace.
+static __device__ __align__(256) int g_splitk_scratch[W4A8_NOALLOC_SCRATCH_BYTES / 4];
+
+// Device address of g_splitk_scratch, looked up once per device.
+int* noalloc_scratch() {
+  static int* cached[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!cached[dev]) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_splitk_scratch) != cudaSuccess) return nullptr;
+    cached[dev] = static_cast<int*>(ptr);
+  }
+  return cached[dev];
+}
+}  // namespace
+
+extern "C" int w4a8_gemm_splitk_noalloc(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int w_kind,
+                                        int M, int N, int K, const w4a8_epilogue* epi, void* C, int64_t ldc,
+                                        void* stream) {
+  bool empty = false;
+  if (int rc = check_gemm(A, lda, W, ldw, w_kind, M, N, K, epi, C, ldc, &empty)) return rc;
+  if (empty) return W4A8_OK;
+  if (w_kind != W4A8_W_INT4) return W4A8_ERR_ARG;
+  if (int64_t(M) * int64_t(N) * 4 > int64_t(W4A8_NOALLOC_SCRATCH_BYTES)) return W4A8_ERR_ARG;
+  int* scratch = noalloc_scratch();
+  if (!scratch) return W4A8_ERR_LAUNCH;
+  const int sms = device_sms();
+  const int tiles_m = (M + kBM - 1) / kBM;
+  int bn = N > 128 ? 256 : (N > 64 ? 128 : 64);
+  while (bn > 64 && tiles_m * ((N + bn - 1) / bn) < sms) bn >>= 1;
+  // gemm_w4 zeroes the M x N sums it uses (cudaMemsetAsync) before the kernel.
+  return gemm_w4(A, lda, W, ldw, M, N, K, epi, C, ldc, bn, sms, scratch, W4A8_NOALLOC_SCRATCH_BYTES,
+                 static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int w4a8_gemm(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int w_kind, int M, int N,
                          int K, const w4a8_epilogue* epi, void* C, int64_t ldc, void* stream) {
   bool empty = false;

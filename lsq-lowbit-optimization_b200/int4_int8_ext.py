@@ -80,6 +80,8 @@ _SIGNATURES = {
     "w4a8_gemm_splitk": [_vp, _i64, _vp, _i64, _int, _int, _int, _int, ctypes.POINTER(Epilogue), _vp, _i64, _vp,
                          ctypes.c_size_t, _vp],
     "w4a8_gemm_splitk_workspace": [_int, _int, _int, _int, ctypes.POINTER(ctypes.c_size_t)],
+    "w4a8_gemm_splitk_noalloc": [_vp, _i64, _vp, _i64, _int, _int, _int, _int, ctypes.POINTER(Epilogue), _vp, _i64,
+                                 _vp],
     "w4a8_conv2d": [_vp, _vp, _int, _i64, ctypes.POINTER(ConvGeom), ctypes.POINTER(Epilogue), _vp, _vp],
     "w4a8_quantize_rows": [_vp, _i64, _vp, _i64, _i64, _int, _f32, _int, _int, _vp],
     "w4a8_quantize_nchw_to_nhwc": [_vp, _vp, _int, _int, _int, _int, _int, _f32, _int, _int, _vp],
@@ -93,6 +95,9 @@ _SIGNATURES = {
     "w4a8_num_sms": [],
 }
 ABI_VERSION = 2
+# w4a8_status (include/w4a8.h)
+OK, ERR_ARG, ERR_ALIGN, ERR_UNSUPPORTED, ERR_TENSORMAP, ERR_LAUNCH, ERR_DEVICE = 0, 1, 2, 3, 4, -1, -2
+NOALLOC_SCRATCH_BYTES = 4 << 20  # W4A8_NOALLOC_SCRATCH_BYTES (include/w4a8.h)
 
 _lib_handle: Optional[ctypes.CDLL] = None
 
