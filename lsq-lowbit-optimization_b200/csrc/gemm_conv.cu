@@ -539,12 +539,19 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
     cp.tiles_h = (g->ho + kTileH - 1) / kTileH;
     cp.tiles_w = (g->wo + kTileW - 1) / kTileW;
   }
+  // Outputs of at most 8x8 at stride 1 (ResNet's 7x7 stage) fill a 16x8
+  // tile to 38%: such tiles hold two images instead (each an 8x8 block).
+  cp.n = g->n;
+  cp.pack2 = (!g->pool && s == 1 && g->ho <= 8 && g->wo <= kTileW) ? 1 : 0;
+  const int sub_h = cp.pack2 ? kTileH / 2 : kTileH;  // output rows per image in a tile
+  if (cp.pack2) cp.tiles_h = cp.tiles_w = 1;
+  const int img_mult = cp.pack2 ? 2 : 1;              // images interleaved in a halo row
   cp.cg = cg;
   cp.a_layout = cg == 128 ? kLayoutSw128 : cg == 64 ? kLayoutSw64 : cg == 32 ? kLayoutSw32 : kLayoutNone;
   cp.halo_w = kTileW + span_w;
-  cp.halo_h = kTileH + span_h;
+  cp.halo_h = sub_h + span_h;
   if (cp.halo_w > 256 || cp.halo_h > 256) return W4A8_ERR_UNSUPPORTED;
-  cp.slot_bytes = (uint32_t(cp.halo_w * cp.halo_h * cg) + 1023u) & ~1023u;
+  cp.slot_bytes = (uint32_t(img_mult * cp.halo_w * cp.halo_h * cg) + 1023u) & ~1023u;
   int slot_of[2][2] = {{-1, -1}, {-1, -1}};
   int slot_py[4], slot_px[4];
   int ns = 0;
@@ -560,7 +567,7 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
       }
   cp.n_slots = ns;
   cp.halo_bytes = (cp.slot_bytes * ns + 1023u) & ~1023u;
-  cp.halo_tx_bytes = uint32_t(ns * cp.halo_w * cp.halo_h * cg);
+  cp.halo_tx_bytes = uint32_t(ns * img_mult * cp.halo_w * cp.halo_h * cg);
   cp.kb_per_group = kbpg;
   auto chunk_off = [&](int k) -> long long {
     const int t = k / cg, within = k % cg;
@@ -569,7 +576,7 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
     const int qy = floordiv(dy, s), py = dy - qy * s;
     const int qx = floordiv(dx, s), px = dx - qx * s;
     const int sl = slot_of[py][px];
-    const int pix = (qy - qmin_h[py]) * cp.halo_w + (qx - qmin_w[px]);
+    const int pix = (qy - qmin_h[py]) * img_mult * cp.halo_w + (qx - qmin_w[px]);
     return (long long)sl * cp.slot_bytes + (long long)pix * cg + within;
   };
   // One operand descriptor per 32-byte K-step, relative to the halo stage
@@ -593,7 +600,7 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   p.M = 0;
   p.N = g->o;
   p.num_kb = groups * kbpg;
-  p.tiles_m = g->n * cp.tiles_h * cp.tiles_w;
+  p.tiles_m = cp.pack2 ? (g->n + 1) / 2 : g->n * cp.tiles_h * cp.tiles_w;
   p.tiles_n = (g->o + bn - 1) / bn;
   p.a_stage_bytes = 0;
   p.b_stage_bytes = bn * kBK;
@@ -662,11 +669,15 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
     const int py = slot_py[sl], px = slot_px[sl];
     const int8_t* base = x + ((long long)py * g->w + px) * g->c;
     // (channels of the group, group, W, H, N); stride phases double W/H strides.
-    const uint64_t dims[5] = {uint64_t(cg), uint64_t(groups), uint64_t((g->w - px + s - 1) / s),
-                              uint64_t((g->h - py + s - 1) / s), uint64_t(g->n)};
-    const uint64_t str[4] = {uint64_t(cg), uint64_t(s) * g->c, uint64_t(s) * g->w * g->c,
-                             uint64_t(g->h) * g->w * g->c};
-    const uint32_t box[5] = {uint32_t(cg), 1, uint32_t(cp.halo_w), uint32_t(cp.halo_h), 1};
+    // Two-image tiles order the dims (c, group, W, N, H): one box then lands
+    // the two images' halo rows interleaved.
+    const uint64_t wd = uint64_t((g->w - px + s - 1) / s), hd = uint64_t((g->h - py + s - 1) / s);
+    const uint64_t ws = uint64_t(s) * g->c, hs = uint64_t(s) * g->w * g->c, ns_ = uint64_t(g->h) * g->w * g->c;
+    const uint64_t dims[5] = {uint64_t(cg), uint64_t(groups), wd, cp.pack2 ? uint64_t(g->n) : hd,
+                              cp.pack2 ? hd : uint64_t(g->n)};
+    const uint64_t str[4] = {uint64_t(cg), ws, cp.pack2 ? ns_ : hs, cp.pack2 ? hs : ns_};
+    const uint32_t box[5] = {uint32_t(cg), 1, uint32_t(cp.halo_w), cp.pack2 ? 2u : uint32_t(cp.halo_h),
+                             cp.pack2 ? uint32_t(cp.halo_h) : 1u};
     if (encode_u8(&tH[sl], base, 5, dims, str, box, swz)) return W4A8_ERR_TENSORMAP;
   }
   const int grid = std::min(p.tiles_m * p.tiles_n, sms);

@@ -97,6 +97,10 @@ struct ConvParams {
   int slot_qh[4], slot_qw[4];  // per slot: TMA start offset in phase-view units
   int kb_per_group;
   int pool;                // 1: fused 3x3/s2/p1 max pool (tiles overlap by one row/column)
+  int pack2;               // 1: a tile holds two images' 8x8 outputs (stride 1, outputs <= 8x8):
+                           //    the halo interleaves the images row by row, MMA row group g is
+                           //    output row g / 2 of image 2 * tile + g % 2
+  int n;                   // images
   int pho, pwo;            // pooled output size
   uint32_t pool_off;       // smem offset of the int32 accumulator staging tile
   // A-operand descriptor of each 32-byte K-step relative to the halo stage
@@ -473,6 +477,13 @@ __device__ __forceinline__ bool row_coords(const KParams& p, int mt, int m, long
     return row < p.M;
   } else {
     const ConvParams& c = p.conv;
+    if (c.pack2) {
+      const int img = 2 * mt + ((m >> 3) & 1), oh = m >> 4, ow = m & 7;
+      const long long pix = (long long)oh * c.wo + ow;
+      out_off = (long long)img * p.epi.s_img + pix * p.epi.s_pix;
+      prow = (long long)img * c.ho * c.wo + pix;
+      return img < c.n && oh < c.ho && ow < c.wo;
+    }
     const int per_img = c.tiles_h * c.tiles_w;
     const int img = mt / per_img;
     const int rem = mt - img * per_img;
@@ -681,8 +692,12 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
               uint8_t* hdst = base + p.h_off + hs * p.conv.halo_bytes;
               for (int sl = 0; sl < p.conv.n_slots; ++sl) {
                 const CUtensorMap* m = sl == 0 ? &tmH0 : sl == 1 ? &tmH1 : sl == 2 ? &tmH2 : &tmH3;
-                tma_load_5d(hdst + sl * p.conv.slot_bytes, m, &bar_hfull[hs], 0, g, ow0 + p.conv.slot_qw[sl],
-                            oh0 + p.conv.slot_qh[sl], img);
+                if (p.conv.pack2)  // map dims (c, group, W, N, H): both images' halo rows, interleaved
+                  tma_load_5d(hdst + sl * p.conv.slot_bytes, m, &bar_hfull[hs], 0, g, ow0 + p.conv.slot_qw[sl],
+                              2 * img, oh0 + p.conv.slot_qh[sl]);
+                else
+                  tma_load_5d(hdst + sl * p.conv.slot_bytes, m, &bar_hfull[hs], 0, g, ow0 + p.conv.slot_qw[sl],
+                              oh0 + p.conv.slot_qh[sl], img);
               }
               if (++hs == p.halo_stages) { hs = 0; hph ^= 1; }
             }
