@@ -539,10 +539,11 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
     cp.tiles_h = (g->ho + kTileH - 1) / kTileH;
     cp.tiles_w = (g->wo + kTileW - 1) / kTileW;
   }
-  // Outputs of at most 8x8 at stride 1 (ResNet's 7x7 stage) fill a 16x8
-  // tile to 38%: such tiles hold two images instead (each an 8x8 block).
+  // Outputs of at most 8x8 (ResNet's 7x7 stage) fill a 16x8 tile to 38%:
+  // such tiles hold two images instead (each an 8x8 block; with stride 2
+  // every phase view is packed the same way).
   cp.n = g->n;
-  cp.pack2 = (!g->pool && s == 1 && g->ho <= 8 && g->wo <= kTileW) ? 1 : 0;
+  cp.pack2 = (!g->pool && g->ho <= 8 && g->wo <= kTileW) ? 1 : 0;
   const int sub_h = cp.pack2 ? kTileH / 2 : kTileH;  // output rows per image in a tile
   if (cp.pack2) cp.tiles_h = cp.tiles_w = 1;
   const int img_mult = cp.pack2 ? 2 : 1;              // images interleaved in a halo row

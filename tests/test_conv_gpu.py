@@ -56,6 +56,11 @@ CONV_CASES = [
     (2, 14, 14, 256, 512, 3, 2, 1),
     (2, 56, 56, 64, 128, 1, 2, 0),
     (2, 14, 14, 256, 512, 1, 2, 0),
+    # two-image tiles (outputs <= 8x8): odd image count, ragged 5x6 / 3x3 outputs, stride 2 phases
+    (3, 7, 7, 128, 64, 3, 1, 1),
+    (3, 5, 6, 64, 128, 3, 1, 1),
+    (5, 13, 11, 128, 128, 3, 2, 1),
+    (3, 6, 6, 64, 64, 1, 2, 0),
     (2, 9, 13, 32, 48, 1, 1, 0),
     (2, 11, 9, 32, 80, 3, 1, 1),
     (2, 9, 9, 384, 64, 3, 2, 1),
