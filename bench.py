@@ -181,6 +181,44 @@ def gemm_tops(device) -> dict:
     return {"shape_mnk": [m, n, k], "ms": round(ms, 4), "tops": round(tops, 1)}
 
 
+def small_m_gemm_hbm(device, hbm_gbs: float) -> list:
+    """Memory-bound W4A8 GEMMs (N = K = 8192, packed weights 32 MiB): M = 1
+    on the CUDA-core GEMV, M = 32 on swapped-operand split-K. L2 (126 MB) is
+    flushed before every timed call by reading a 256 MiB buffer (clean lines,
+    so no write-back lands inside the timed call) and the weights stream from
+    HBM; only the GEMM itself is inside the events."""
+    import int4_int8_ext as ext
+
+    n = k = 8192
+    gen = torch.Generator(device=device).manual_seed(1)
+    w = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=device, generator=gen)
+    flush = torch.ones(256 << 20, dtype=torch.uint8, device=device)
+    out = []
+    for m in (1, 32):
+        a = torch.randint(-128, 128, (m, k), dtype=torch.int8, device=device, generator=gen)
+        c = torch.empty((m, n), dtype=torch.int32, device=device)
+        epi = ext.make_epilogue(ext.OUT_S32)
+        for _ in range(3):
+            ext.gemm(a, w, ext.W_INT4, k, epi, c)
+        total = 0.0
+        iters = 20
+        for _ in range(iters):
+            flush_sum = flush.max()  # noqa: F841 (read-only L2 flush)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            ext.gemm(a, w, ext.W_INT4, k, epi, c)
+            e1.record()
+            torch.cuda.synchronize()
+            total += e0.elapsed_time(e1)
+        ms = total / iters
+        nbytes = w.numel() + a.numel() + c.numel() * 4
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out.append({"shape_mnk": [m, n, k], "path": "gemv" if m <= 8 else "split-k",
+                    "us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm_gbs, 4),
+                    "l2": "flushed before each call (256 MiB read)"})
+    return out
+
+
 def fp16_cudnn_rate(device, batch: int, arch: str) -> dict:
     """The same network in FP16 through torchvision + cuDNN (channels_last,
     cudnn.benchmark, CUDA graph): the library path the W4A8 model must beat."""
@@ -333,6 +371,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             g.update(frac_of_int8_peak=round(g["tops"] / int8_peak, 4),
                      frac_of_nominal=round(g["tops"] / INT8_NOMINAL_TOPS, 4))
             line["gemm_int8"] = g
+            line["gemm_small_m"] = small_m_gemm_hbm(device, peaks["hbm_gbs"])
             fp16 = fp16_cudnn_rate(device, B, args.arch)
             fp16["w4a8_speedup"] = round(value / fp16["value"], 3)
             line["fp16_cudnn"] = fp16
