@@ -170,14 +170,16 @@ bool use_gemv(int M, int K) {
   return M >= 1 && M <= kGemvMaxTokens && K % 64 == 0 && gemv_smem_bytes(kGemvMaxTokens, K) <= 200 * 1024;
 }
 
-template <int MT>
+template <int MT, bool ROWS>
 int launch_gemv_t(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K,
                   const EpiParams& e, cudaStream_t st) {
-  auto kern = w4a8_gemv_w4_kernel<MT>;
-  const size_t smem = gemv_smem_bytes(MT, K);
+  auto kern = ROWS ? w4a8_gemv_w4_rows_kernel<MT> : w4a8_gemv_w4_kernel<MT>;
+  const size_t smem = ROWS ? gemv_rows_smem_bytes(MT, K) : gemv_smem_bytes(MT, K);
   if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return W4A8_ERR_LAUNCH;
-  kern<<<unsigned((N + 31) / 32), kGemvWarps * 32, smem, st>>>(A, lda, static_cast<const uint8_t*>(W), ldw, M, N, K, e);
+  const int per_block = ROWS ? kGemvRows : 32;
+  kern<<<unsigned((N + per_block - 1) / per_block), kGemvWarps * 32, smem, st>>>(
+      A, lda, static_cast<const uint8_t*>(W), ldw, M, N, K, e);
   return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH;
 }
 
@@ -190,10 +192,10 @@ int gemv_w4(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int M, int
   e.s_img = 0;
   e.s_pix = ldc;
   e.s_ch = 1;
-  if (M <= 1) return launch_gemv_t<1>(A, lda, W, ldw, M, N, K, e, st);
-  if (M <= 2) return launch_gemv_t<2>(A, lda, W, ldw, M, N, K, e, st);
-  if (M <= 4) return launch_gemv_t<4>(A, lda, W, ldw, M, N, K, e, st);
-  return launch_gemv_t<8>(A, lda, W, ldw, M, N, K, e, st);
+  if (M <= 1) return launch_gemv_t<1, true>(A, lda, W, ldw, M, N, K, e, st);
+  if (M <= 2) return launch_gemv_t<2, true>(A, lda, W, ldw, M, N, K, e, st);
+  if (M <= 4) return launch_gemv_t<4, false>(A, lda, W, ldw, M, N, K, e, st);
+  return launch_gemv_t<8, false>(A, lda, W, ldw, M, N, K, e, st);
 }
 
 // Split-K plan for a small-M (<= 128) W4 GEMM whose output tiles alone

@@ -832,6 +832,18 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
     int it = set;
     for (int t = blockIdx.x + set * gridDim.x; t < total_tiles; t += kNB * gridDim.x, it += kNB) {
       const int buf = set;
+      if (p.epi.residual && !(kConv && p.conv.pool)) {
+        // The float32 identity rows of this thread's pixel are pulled into L2
+        // while the MMA still works on the tile, so the epilogue's loads hit.
+        const int mt0 = t / p.tiles_n, nt0 = t - mt0 * p.tiles_n;
+        long long o0 = 0, pr0 = 0;
+        if (row_coords<kConv>(p, mt0, m, o0, pr0)) {
+          const char* r = reinterpret_cast<const char*>(p.epi.residual + pr0 * p.epi.res_ld + nt0 * BN);
+          const int nbytes = 4 * min(BN, p.epi.n_total - nt0 * BN);
+          for (int off = slice * 128; off < nbytes; off += 128 * kSlices)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(r + off));
+        }
+      }
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&bar_tfull[buf], (it / kNB) & 1, &abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
