@@ -85,6 +85,68 @@ __global__ void s2d_q_kernel(const float* __restrict__ x, int8_t* __restrict__ y
   }
 }
 
+// clamp(rint(x / s), qn, qp) without a division per element: t = x * fl(1/s)
+// differs from fl(x/s) by at most |x/s| * 3.1 * 2^-24 (< 6.1e-5 for |t| < 256),
+// so rint agrees unless t lies within that distance of a half-integer; inside
+// a 2^-12 guard band the exact quotient is taken. |t| >= 256 always clamps.
+__device__ __forceinline__ int quant_rs(float x, float scale, float rs, float qnf, float qpf) {
+  float t = __fmul_rn(x, rs);
+  if (fabsf(t) < 256.0f) {
+    const float rt = __fsub_rn(__fadd_rn(t, 12582912.0f), 12582912.0f);
+    if (fabsf(fabsf(__fsub_rn(t, rt)) - 0.5f) < 2.44140625e-4f) t = __fdiv_rn(x, scale);
+  }
+  t = fminf(fmaxf(t, qnf), qpf);
+  return __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
+}
+
+// Space-to-depth by 2 + quantise, vectorised: a thread makes output pixels
+// 2j and 2j + 1 of one row from six coalesced float4 loads (3 channels x 2
+// input rows, 4 consecutive columns each). Needs c == 3, cp == 16, w % 4 == 0
+// and a 16-byte aligned x.
+__global__ void __launch_bounds__(256) s2d_q3_vec_kernel(const float* __restrict__ x, int8_t* __restrict__ y, int n,
+                                                         int h, int w, float scale, float rs, int qn, int qp) {
+  const int ho = h / 2, wq = w / 4;  // wq thread columns of two output pixels each
+  const long long total = (long long)n * ho * wq;
+  const float qnf = float(qn), qpf = float(qp);
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int j = int(i % wq);
+    const long long t = i / wq;
+    const int Y = int(t % ho);
+    const int img = int(t / ho);
+    float4 v[3][2];
+#pragma unroll
+    for (int cc = 0; cc < 3; ++cc)
+#pragma unroll
+      for (int dy = 0; dy < 2; ++dy)
+        v[cc][dy] = __ldcs(reinterpret_cast<const float4*>(x + (((long long)img * 3 + cc) * h + 2 * Y + dy) * w) + j);
+    // Channel (dy * 2 + dx) * 3 + cc of pixel p (columns 4j + 2p + dx).
+    uint32_t out[2][4];
+#pragma unroll
+    for (int pp = 0; pp < 2; ++pp) {
+      int q[12];
+#pragma unroll
+      for (int dy = 0; dy < 2; ++dy)
+#pragma unroll
+        for (int dx = 0; dx < 2; ++dx)
+#pragma unroll
+          for (int cc = 0; cc < 3; ++cc) {
+            const float4& f = v[cc][dy];
+            const float e = pp == 0 ? (dx == 0 ? f.x : f.y) : (dx == 0 ? f.z : f.w);
+            q[(dy * 2 + dx) * 3 + cc] = quant_rs(e, scale, rs, qnf, qpf);
+          }
+#pragma unroll
+      for (int wd = 0; wd < 3; ++wd)
+        out[pp][wd] = (uint32_t(q[4 * wd]) & 0xFFu) | ((uint32_t(q[4 * wd + 1]) & 0xFFu) << 8) |
+                      ((uint32_t(q[4 * wd + 2]) & 0xFFu) << 16) | ((uint32_t(q[4 * wd + 3]) & 0xFFu) << 24);
+      out[pp][3] = 0;
+    }
+    uint4* dst = reinterpret_cast<uint4*>(y + (((long long)img * ho + Y) * (w / 2) + 2 * j) * 16);
+    dst[0] = make_uint4(out[0][0], out[0][1], out[0][2], out[0][3]);
+    dst[1] = make_uint4(out[1][0], out[1][1], out[1][2], out[1][3]);
+  }
+}
+
 // Reference explicit lowering: cols[row, c*9 + ky*3 + kx]; out-of-image
 // taps quantise 0.0, columns >= c*9 are 0.
 __global__ void lower_q3x3_kernel(const float* __restrict__ x, int8_t* __restrict__ cols, int n, int c, int h,
@@ -228,6 +290,12 @@ extern "C" int w4a8_s2d_quantize(const float* x, int8_t* y, int n, int c, int h,
   if (!x || !y) return W4A8_ERR_ARG;
   if (reinterpret_cast<uintptr_t>(y) & 15) return W4A8_ERR_ALIGN;
   const long long total = (long long)n * (h / 2) * (w / 2);
+  if (c == 3 && c_pad == 16 && w % 4 == 0 && h % 2 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const long long threads = (long long)n * (h / 2) * (w / 4);
+    const float rs = 1.0f / scale;  // IEEE single division on the host: fl(1/s), as the guard band assumes
+    s2d_q3_vec_kernel<<<grid_for(threads, 256), 256, 0, (cudaStream_t)stream>>>(x, y, n, h, w, scale, rs, qn, qp);
+    return finish();
+  }
   s2d_q_kernel<<<grid_for(total, 128), 128, 0, (cudaStream_t)stream>>>(x, y, n, c, h, w, c_pad, scale, qn, qp);
   return finish();
 }

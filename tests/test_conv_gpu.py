@@ -113,6 +113,32 @@ def test_module_matches_reference_golden(cuda):
         assert_equal(y, d[f"{name}_y"], f"module {name} vs reference")
 
 
+def test_s2d_quantize_matches_oracle(cuda):
+    """fp32 NCHW images -> int8 space-to-depth codes (channel (dy*2+dx)*3+c,
+    padded to 16): clamp(rint(x / s)) in IEEE float32, checked on values at
+    and next to the half-integer rounding boundaries and past the clamp."""
+    g = rng(31)
+    n, c, h, w, s, qn, qp = 2, 3, 32, 40, 0.05, -128, 127
+    x = g.normal(0, 3, (n, c, h, w)).astype(np.float32)
+    half = ((np.arange(-140, 140) + 0.5) * np.float32(s)).astype(np.float32)
+    edge = np.concatenate([half, np.nextafter(half, np.float32(np.inf)), np.nextafter(half, np.float32(-np.inf)),
+                           np.float32([1e3, -1e3, 6.4, -6.4, 6.45, -6.45])])
+    flat = x.reshape(-1)
+    flat[:edge.size] = edge
+    q = np.clip(np.rint(x / np.float32(s)), qn, qp).astype(np.int8)
+    want = np.zeros((n, h // 2, w // 2, 16), np.int8)
+    for dy in range(2):
+        for dx in range(2):
+            for cc in range(c):
+                want[..., (dy * 2 + dx) * 3 + cc] = q[:, cc, dy::2, dx::2]
+    xd = to_dev(x, cuda)
+    got = torch.full((n, h // 2, w // 2, 16), 99, dtype=torch.int8, device=cuda)
+    rc = ext.lib().w4a8_s2d_quantize(xd.data_ptr(), got.data_ptr(), n, c, h, w, 16, s, qn, qp,
+                                     torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    assert_equal(got, want, "s2d quantize")
+
+
 def test_stem_s2d_conv(cuda):
     """4x4 conv, pad 2 top/left, 16 channels: the space-to-depth stem."""
     g = rng(77)
