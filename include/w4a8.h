@@ -121,16 +121,27 @@ W4A8_API int w4a8_gemm_splitk(const int8_t* A, int64_t lda, const void* W, int64
 W4A8_API int w4a8_gemm_splitk_workspace(int M, int N, int K, int w_kind, size_t* bytes);
 
 /*
- * w4a8_gemm_splitk without a workspace argument and without allocating:
- * the int32 partial sums live in a fixed device array of
- * W4A8_NOALLOC_SCRATCH_BYTES inside the library (located once per device,
- * cleared by every call). INT4 weights only; shapes with M * N * 4 above
- * W4A8_NOALLOC_SCRATCH_BYTES are rejected with W4A8_ERR_ARG. Results equal
- * w4a8_gemm. All calls on a device share the one array, so calls that
- * overlap in time (different streams, or host threads) race and corrupt
- * each other's results: order them on one stream.
- * No counterpart in the reference (its int4_int8_gemm path,
- * csrc/int4_int8_kernels.cu:257-291, has neither split-K nor a workspace).
+ * w4a8_gemm_splitk for callers that cannot allocate device memory. Examples
+ * are plugins and serving runtimes whose device memory belongs to the host
+ * application's own pool or fixed budget: there a cudaMalloc can fail or
+ * break the budget, and cudaMalloc / cudaFree synchronise the whole device,
+ * stalling every other stream. This entry point needs no workspace. The
+ * caller passes only inputs and outputs, and the int32 split-K partial sums
+ * go to one fixed array of W4A8_NOALLOC_SCRATCH_BYTES (4 MiB) inside the
+ * library. Every GPU that loads the library holds that array until the
+ * process exits.
+ * - INT4 weights only. Shapes with M * N * 4 above
+ *   W4A8_NOALLOC_SCRATCH_BYTES are rejected with W4A8_ERR_ARG and nothing
+ *   is launched.
+ * - Results equal w4a8_gemm.
+ * - The first call on a device looks up the array's device address (once per
+ *   device, with that device current). Make that first call before any
+ *   stream capture.
+ * - Each call clears the part of the array it uses.
+ * - All calls on a device share the one array, so calls that overlap on the
+ *   GPU (different streams, or several host threads) race and corrupt each
+ *   other's results. Order them on one stream.
+ * No counterpart in the reference.
  */
 #define W4A8_NOALLOC_SCRATCH_BYTES (4u << 20)
 W4A8_API int w4a8_gemm_splitk_noalloc(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int w_kind, int M,

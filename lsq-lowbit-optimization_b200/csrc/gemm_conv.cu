@@ -367,11 +367,15 @@ extern "C" int w4a8_gemm_splitk(const int8_t* A, int64_t lda, const void* W, int
 }
 
 namespace {
-// Scratch of w4a8_gemm_splitk_noalloc: the split-K int32 partial sums live in
-// this fixed device array instead of a caller or allocator workspace.
+// Scratch of w4a8_gemm_splitk_noalloc, for callers that cannot allocate
+// device memory: the split-K int32 partial sums live in this fixed array
+// instead of a workspace. Every GPU that loads the library holds it until the
+// process exits. In host code the name is only a stand-in for the symbol, not
+// a device address: kernels get the address from noalloc_scratch().
 static __device__ __align__(256) int g_splitk_scratch[W4A8_NOALLOC_SCRATCH_BYTES / 4];
 
-// Device address of g_splitk_scratch, looked up once per device.
+// Device address of g_splitk_scratch on the current device, looked up on the
+// first call per device (cudaGetSymbolAddress, return code checked) and cached.
 int* noalloc_scratch() {
   static int* cached[64] = {nullptr};
   int dev = 0;

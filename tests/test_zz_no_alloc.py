@@ -1,9 +1,13 @@
 """The allocation-free split-K GEMM entry point (w4a8_gemm_splitk_noalloc).
 
-Its int32 partial sums live in a fixed device array inside the library, so
-two calls in a row must each clear it: both are checked bit-exact against the
-workspace-taking entry point (w4a8_gemm_splitk) and the oracle. This file is
-collected last and must pass on its own as well as after the other tests.
+Some callers cannot allocate device memory: plugins and serving runtimes
+whose device memory belongs to the host application's pool or fixed budget,
+where cudaMalloc can fail and cudaMalloc / cudaFree synchronise the device.
+This entry point takes only inputs and outputs. Its int32 partial sums live in
+a fixed device array inside the library, so two calls in a row must each clear
+it. Both calls are checked bit-exact against the workspace-taking entry point
+(w4a8_gemm_splitk) and the oracle. This file is collected last and must pass
+on its own as well as after the other tests.
 """
 import ctypes
 
