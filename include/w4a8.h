@@ -164,7 +164,7 @@ typedef struct {
   int out_layout;    /* W4A8_LAYOUT_NHWC or W4A8_LAYOUT_NCHW */
   int64_t ldo;       /* NHWC: output elements per pixel (>= o) */
   int pool;          /* 1: fuse a 3x3/s2/p1 max pool after the epilogue
-                        (o <= 64, NHWC out); outputs are then pooled, of size
+                        (8-bit weights, o <= 64, NHWC out); outputs are then pooled, of size
                         ((ho-1)/2+1, (wo-1)/2+1). 0: no pooling. */
 } w4a8_conv_geom;
 

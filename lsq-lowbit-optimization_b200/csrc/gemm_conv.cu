@@ -488,7 +488,7 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   if (g->out_layout != W4A8_LAYOUT_NHWC && g->out_layout != W4A8_LAYOUT_NCHW) return W4A8_ERR_ARG;
   if (g->out_layout == W4A8_LAYOUT_NHWC && g->ldo < g->o) return W4A8_ERR_ARG;
   if (g->pool != 0 && g->pool != 1) return W4A8_ERR_ARG;
-  if (g->pool && (g->o > 64 || g->out_layout != W4A8_LAYOUT_NHWC || epi->residual ||
+  if (g->pool && (i4 || g->o > 64 || g->out_layout != W4A8_LAYOUT_NHWC || epi->residual ||
                   (epi->out_kind != W4A8_OUT_S8 && epi->out_kind != W4A8_OUT_F32) || (g->o % 4)))
     return W4A8_ERR_UNSUPPORTED;
   if (g->n == 0) return W4A8_OK;
@@ -576,6 +576,7 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   cp.halo_bytes = (cp.slot_bytes * ns + 1023u) & ~1023u;
   cp.halo_tx_bytes = uint32_t(ns * img_mult * cp.halo_w * cp.halo_h * cg);
   cp.kb_per_group = kbpg;
+  cp.tail_steps = (taps * cg + 31) / 32 - (kbpg - 1) * (kBK / 32);
   auto chunk_off = [&](int k) -> long long {
     const int t = k / cg, within = k % cg;
     const int ky = t / g->kw, kx = t % g->kw;

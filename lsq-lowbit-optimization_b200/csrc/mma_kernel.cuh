@@ -96,6 +96,7 @@ struct ConvParams {
   uint32_t halo_tx_bytes;  // bytes the TMA loads of one stage deliver
   int slot_qh[4], slot_qw[4];  // per slot: TMA start offset in phase-view units
   int kb_per_group;
+  int tail_steps;          // real 32-byte K-steps in a group's last k-block (1..4)
   int pool;                // 1: fused 3x3/s2/p1 max pool (tiles overlap by one row/column)
   int pack2;               // 1: a tile holds two images' 8x8 outputs (stride 1, outputs <= 8x8):
                            //    the halo interleaves the images row by row, MMA row group g is
@@ -537,18 +538,31 @@ __device__ __forceinline__ void pool_epilogue(const KParams& p, const EpiConsts&
     const int pr = th * kPoolRows + pr_l, pc = tw * kPoolCols + pc_l;
     const int ch = quad * 4;
     if (pr < c.pho && pc < c.pwo && ch < e.n_total) {
-      int mx[4] = {INT_MIN, INT_MIN, INT_MIN, INT_MIN}, mn[4] = {INT_MAX, INT_MAX, INT_MAX, INT_MAX};
+      // Window rows / columns outside the image are clamped to the nearest
+      // inside one; the window centre is always inside, so a clamped index
+      // repeats an element of the same window and leaves max and min as they are.
+      int rr[3], cc[3];
+#pragma unroll
+      for (int d = 0; d < 3; ++d) {
+        rr[d] = min(max(2 * pr_l + d, -oh0), c.ho - 1 - oh0);
+        cc[d] = min(max(2 * pc_l + d, -ow0), c.wo - 1 - ow0);
+      }
+      // Row by row: max / min of the row's three pixels, then of the rows.
+      int mx[4], mn[4];
 #pragma unroll
       for (int dy = 0; dy < 3; ++dy) {
-        const int lr = 2 * pr_l + dy, r = oh0 + lr;
-        if (r < 0 || r >= c.ho) continue;
+        const int* row = stg + rr[dy] * kTileW * kPoolPitch + ch;
+        const int4 v0 = *reinterpret_cast<const int4*>(row + cc[0] * kPoolPitch);
+        const int4 v1 = *reinterpret_cast<const int4*>(row + cc[1] * kPoolPitch);
+        const int4 v2 = *reinterpret_cast<const int4*>(row + cc[2] * kPoolPitch);
+        const int rmx[4] = {__vimax3_s32(v0.x, v1.x, v2.x), __vimax3_s32(v0.y, v1.y, v2.y),
+                            __vimax3_s32(v0.z, v1.z, v2.z), __vimax3_s32(v0.w, v1.w, v2.w)};
+        const int rmn[4] = {__vimin3_s32(v0.x, v1.x, v2.x), __vimin3_s32(v0.y, v1.y, v2.y),
+                            __vimin3_s32(v0.z, v1.z, v2.z), __vimin3_s32(v0.w, v1.w, v2.w)};
 #pragma unroll
-        for (int dx = 0; dx < 3; ++dx) {
-          const int lc = 2 * pc_l + dx, col = ow0 + lc;
-          if (col < 0 || col >= c.wo) continue;
-          const int4 v = *reinterpret_cast<const int4*>(stg + (lr * kTileW + lc) * kPoolPitch + ch);
-          mx[0] = max(mx[0], v.x); mx[1] = max(mx[1], v.y); mx[2] = max(mx[2], v.z); mx[3] = max(mx[3], v.w);
-          mn[0] = min(mn[0], v.x); mn[1] = min(mn[1], v.y); mn[2] = min(mn[2], v.z); mn[3] = min(mn[3], v.w);
+        for (int i = 0; i < 4; ++i) {
+          mx[i] = dy == 0 ? rmx[i] : max(mx[i], rmx[i]);
+          mn[i] = dy == 0 ? rmn[i] : min(mn[i], rmn[i]);
         }
       }
       float y[4];
@@ -773,13 +787,23 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
             tc_fence_after();
             const uint32_t halo_lo = (base_u32 + p.h_off + hs * p.conv.halo_bytes) >> 4;
             if (resident) {
-              for (int i = 0; i < kbpg; ++i, ++kb) {
+              // Resident weights: the zero-weight padding steps of the
+              // group's last k-block are not issued.
+              for (int i = 0; i < kbpg - 1; ++i, ++kb) {
                 const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(kb) * b_step);
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
                   mma_i8_ss(d_tmem, p.conv.step_desc[i * 4 + j] + halo_lo, b_desc0 + 2 * j, idesc,
                             (kb | j) != 0 ? 1u : 0u);
               }
+              const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(kb) * b_step);
+              const int i = kbpg - 1;
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                if (j < p.conv.tail_steps)
+                  mma_i8_ss(d_tmem, p.conv.step_desc[i * 4 + j] + halo_lo, b_desc0 + 2 * j, idesc,
+                            (kb | j) != 0 ? 1u : 0u);
+              ++kb;
             } else {
               for (int i = 0; i < kbpg; ++i, ++kb) {
                 ok &= mbar_wait(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag);
@@ -854,11 +878,13 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       tc_fence_after();
       const int mt = t / p.tiles_n;
       const int nt = t - mt * p.tiles_n;
-      if (kConv && p.conv.pool) {
-        pool_epilogue<BN, kSetWarps>(p, k, tmem_base + (uint32_t(q * 32) << 16) + buf * BN,
-                                     base + p.conv.pool_off + set * kPoolStageBytes, mt, m, slice, kSlices,
-                                     (warp - 4) % kSetWarps, lane, &bar_tempty[buf], 2 + set);
-        continue;
+      if constexpr (kConv && BN == 64 && !kInt4) {  // the fused pool: 8-bit weights, <= 64 channels
+        if (p.conv.pool) {
+          pool_epilogue<BN, kSetWarps>(p, k, tmem_base + (uint32_t(q * 32) << 16) + buf * BN,
+                                       base + p.conv.pool_off + set * kPoolStageBytes, mt, m, slice, kSlices,
+                                       (warp - 4) % kSetWarps, lane, &bar_tempty[buf], 2 + set);
+          continue;
+        }
       }
       long long out_off = 0, prow = 0;
       const bool valid = row_coords<kConv>(p, mt, m, out_off, prow);

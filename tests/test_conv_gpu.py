@@ -213,11 +213,13 @@ def test_lower_quantize_3x3_matches_oracle(cuda):
     assert_equal(got, orc.lower_quantize_3x3(x, 0.05, 2, 127, 46), "lowering qn>0")
 
 
-def test_conv_fused_maxpool(cuda):
+@pytest.mark.parametrize("h,w", [(30, 26), (29, 27)])
+def test_conv_fused_maxpool(cuda, h, w):
     """Stem-style conv with the 3x3/s2/p1 max pool fused into the epilogue;
-    alpha has both signs (pooling picks the max or min accumulator)."""
-    g = rng(21)
-    n, h, w, c, o = 2, 30, 26, 16, 64
+    alpha has both signs (pooling picks the max or min accumulator). Odd
+    sizes put the last pooled row / column's window partly outside the image."""
+    g = rng(21 + h)
+    n, c, o = 2, 16, 64
     xq = rand_i8(g, (n, h, w, c))
     wt = rand_i8(g, (o, 4, 4, c))
     alpha = g.uniform(1e-4, 1e-3, o).astype(np.float32)
