@@ -277,8 +277,9 @@ __device__ __forceinline__ void epilogue16_fast(const EpiParams& e, const EpiCon
     t[j] = mul2(y[j], rs2);
     const uint64_t rt = add2(add2(t[j], magic2), neg_magic2);
     const uint64_t d = add2(t[j], rt ^ 0x8000000080000000ull);  // t - rint(t)
-    slow |= (fabsf(flo(t[j])) < 256.0f) & (fabsf(flo(d)) > 0.49975586f);
-    slow |= (fabsf(fhi(t[j])) < 256.0f) & (fabsf(fhi(d)) > 0.49975586f);
+    // Near-ties only; lsq_guard itself skips |t| >= 256, whose codes saturate.
+    slow |= fabsf(flo(d)) > 0.49975586f;
+    slow |= fabsf(fhi(d)) > 0.49975586f;
   }
   if (slow) {
 #pragma unroll

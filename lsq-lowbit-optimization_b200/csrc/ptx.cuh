@@ -68,19 +68,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Spin part of mbar_wait, kept out of line: an inlined spin loop inside the
-// MMA issue loop slows that loop down even when it is never entered.
+// try_wait that may suspend the thread until the phase completes or
+// `suspend_ns` passes, so a waiting warp takes no issue slots meanwhile.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t suspend_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait part of mbar_wait, kept out of line: an inlined wait loop inside the
+// MMA issue loop slows that loop down even when it is never entered. Each
+// try suspends for at most 20 us; the abort flag and the time limit are
+// checked after every try.
 __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   const unsigned long long t0 = global_timer_ns();
-  uint32_t spins = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 255u) == 0) {
-      if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
-        *abort_flag = 1;
-        return false;
-      }
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      return false;
     }
   }
 }
