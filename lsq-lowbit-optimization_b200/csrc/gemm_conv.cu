@@ -621,7 +621,14 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   // The fused pool stages one tile of int32 accumulators (128 x 68 words)
   // per epilogue warp set.
   const uint32_t pool_bytes = g->pool ? uint32_t(acc_buffers(bn, true)) * kPoolStageBytes : 0u;
-  const int budget = kSmemBudget - int(pool_bytes);
+  // The epilogue's shared-memory copies of alpha and beta (not with the pool,
+  // whose epilogue reads them per pooled pixel).
+  cp.ab_pitch = (g->o + 15) & ~15;
+  const uint32_t ab_bytes = (!g->pool && (epi->alpha || epi->beta) && g->o <= 1024)
+                                ? (uint32_t(8 * cp.ab_pitch) + 1023u) & ~1023u
+                                : 0u;
+  const uint32_t fixed_bytes = pool_bytes + ab_bytes;
+  const int budget = kSmemBudget - int(fixed_bytes);
   p.b_resident = 0;
   if (p.tiles_n == 1 && bres_bytes + 2 * cp.halo_bytes <= uint32_t(budget)) {
     p.b_resident = 1;
@@ -634,14 +641,15 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
     p.stages = 0;
     for (int hs = kMaxHaloStages; hs >= 1 && p.stages < 3; --hs) {
       p.halo_stages = hs;
-      p.stages = pick_stages(per_stage, hs * cp.halo_bytes + pool_bytes);
+      p.stages = pick_stages(per_stage, hs * cp.halo_bytes + fixed_bytes);
     }
     if (p.stages < 2) return W4A8_ERR_UNSUPPORTED;
   }
   p.a_off = 0;
   p.h_off = 0;
   cp.pool_off = p.halo_stages * cp.halo_bytes;
-  p.b_off = cp.pool_off + pool_bytes;
+  cp.ab_off = ab_bytes ? cp.pool_off + pool_bytes : 0u;
+  p.b_off = cp.pool_off + pool_bytes + ab_bytes;
   p.bp_off = 0;
   p.tx_bytes = i4 ? p.b_stage_bytes / 2 : p.b_stage_bytes;
   p.tmem_cols = 2 * bn;

@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(kW4Threads, 1)
     int it = set;
     for (int t = tile0 + set * tstep; t < total_tiles; t += kNB * tstep, it += kNB) {
       int ok = 1;
-      if (lane == 0) ok = mbar_wait(&bar_tfull[set], (it >> 1) & 1, &abort_flag) ? 1 : 0;
+      if (lane == 0) ok = mbar_wait_idle(&bar_tfull[set], (it >> 1) & 1, &abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         if (lane == 0) atomicOr(p.err, kErrTimeoutEpilogue);

@@ -96,6 +96,8 @@ struct ConvParams {
   uint32_t halo_tx_bytes;  // bytes the TMA loads of one stage deliver
   int slot_qh[4], slot_qw[4];  // per slot: TMA start offset in phase-view units
   int kb_per_group;
+  uint32_t ab_off;         // smem offset of the epilogue's alpha / beta copies (0: read from global)
+  int ab_pitch;            // floats from the alpha copy to the beta copy
   int tail_steps;          // real 32-byte K-steps in a group's last k-block (1..4)
   int pool;                // 1: fused 3x3/s2/p1 max pool (tiles overlap by one row/column)
   int pack2;               // 1: a tile holds two images' 8x8 outputs (stride 1, outputs <= 8x8):
@@ -190,8 +192,19 @@ __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
 
 // Common-case epilogue for 16 contiguous columns (aligned vectors, NHWC /
 // row-major output): the same arithmetic as epilogue16, on float pairs.
+// 16 bytes from shared memory.
+__device__ __forceinline__ ulonglong2 lds128(const float* p) {
+  ulonglong2 v;
+  asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "r"(smem_u32(p)));
+  return v;
+}
+
+// kSmemAB: sa / sb, when non-null, are shared-memory copies of alpha / beta
+// read in place of e.alpha / e.beta (same values, indexed alike).
+template <bool kSmemAB>
 __device__ __forceinline__ void epilogue16_fast(const EpiParams& e, const EpiConsts& k, const uint32_t* acc, int n,
-                                                long long out_off, long long prow) {
+                                                long long out_off, long long prow, const float* sa,
+                                                const float* sb) {
   constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
   const uint64_t magic2 = fpair(kMagic, kMagic), neg_magic2 = fpair(-kMagic, -kMagic);
   uint64_t y[8];
@@ -214,7 +227,7 @@ __device__ __forceinline__ void epilogue16_fast(const EpiParams& e, const EpiCon
     const ulonglong2* a2 = reinterpret_cast<const ulonglong2*>(e.alpha + n);
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const ulonglong2 v = __ldg(a2 + g);
+      const ulonglong2 v = (kSmemAB && sa) ? lds128(sa + n + 4 * g) : __ldg(a2 + g);
       y[2 * g] = mul2(y[2 * g], v.x);
       y[2 * g + 1] = mul2(y[2 * g + 1], v.y);
     }
@@ -227,7 +240,7 @@ __device__ __forceinline__ void epilogue16_fast(const EpiParams& e, const EpiCon
     const ulonglong2* b2 = reinterpret_cast<const ulonglong2*>(e.beta + n);
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const ulonglong2 v = __ldg(b2 + g);
+      const ulonglong2 v = (kSmemAB && sb) ? lds128(sb + n + 4 * g) : __ldg(b2 + g);
       y[2 * g] = add2(y[2 * g], v.x);
       y[2 * g + 1] = add2(y[2 * g + 1], v.y);
     }
@@ -304,8 +317,12 @@ __device__ __forceinline__ void epilogue16_fast(const EpiParams& e, const EpiCon
 
 // Applies the fused epilogue to 16 accumulators (columns n .. n+15) of one
 // output row; all indexing is static so nothing spills to local memory.
+// kSmemAB: sa / sb (optional) are shared-memory copies of alpha / beta for
+// the vector path (16-byte aligned at every multiple of 16 columns).
+template <bool kSmemAB = false>
 __device__ __forceinline__ void epilogue16(const EpiParams& e, const EpiConsts& k, const uint32_t* acc, int n,
-                                           long long out_off, long long prow) {
+                                           long long out_off, long long prow, const float* sa = nullptr,
+                                           const float* sb = nullptr) {
   const int ncols = min(16, e.n_total - n);
   if (ncols <= 0) return;
   const bool vec = (ncols == 16) && (e.s_ch == 1);
@@ -317,7 +334,7 @@ __device__ __forceinline__ void epilogue16(const EpiParams& e, const EpiConsts& 
         (e.residual ? reinterpret_cast<uintptr_t>(e.residual + prow * e.res_ld + n) : 0) |
         (e.aux ? reinterpret_cast<uintptr_t>(e.aux + prow * e.aux_ld + n) : 0);
     if ((mis & 15) == 0) {
-      epilogue16_fast(e, k, acc, n, out_off, prow);
+      epilogue16_fast<kSmemAB>(e, k, acc, n, out_off, prow, sa, sb);
       return;
     }
   }
@@ -702,7 +719,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
         for (int kb = 0; ok && kb < p.num_kb; ++kb) {
           if constexpr (kConv) {
             if (kb_in_g == 0) {
-              if (!mbar_wait(&bar_hempty[hs], hph ^ 1, &abort_flag)) { ok = false; break; }
+              if (!mbar_wait_t<kConv>(&bar_hempty[hs], hph ^ 1, &abort_flag)) { ok = false; break; }
               mbar_arrive_expect_tx(&bar_hfull[hs], p.conv.halo_tx_bytes);
               uint8_t* hdst = base + p.h_off + hs * p.conv.halo_bytes;
               for (int sl = 0; sl < p.conv.n_slots; ++sl) {
@@ -721,7 +738,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
             if (++kb_in_g == kbpg) { kb_in_g = 0; ++g; }
             continue;
           }
-          if (!mbar_wait(&bar_empty[s], ph ^ 1, &abort_flag)) { ok = false; break; }
+          if (!mbar_wait_t<kConv>(&bar_empty[s], ph ^ 1, &abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&bar_full[s], p.tx_bytes);
           if constexpr (!kConv)
             tma_load_2d(base + p.a_off + s * p.a_stage_bytes, &tmA, &bar_full[s], kb * kBK, mt * kBM);
@@ -770,21 +787,21 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       uint32_t ph = 0, hph = 0;
       bool ok = true;
       const bool resident = kConv && p.b_resident;
-      if (resident) ok = mbar_wait(kInt4 ? &bar_bready : &bar_bres, 0, &abort_flag);
+      if (resident) ok = mbar_wait_t<kConv>(kInt4 ? &bar_bready : &bar_bres, 0, &abort_flag);
       // The inner loops carry no break: a failed wait clears `ok` and sets the
       // CTA's abort flag (so every later wait gives up within a few hundred
       // polls), the tile's remaining MMAs read in-bounds shared memory, and
       // the tile loop stops. Inner loops without exits issue markedly faster.
       for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x, ++it) {
         const int buf = it % kNB;
-        if (!mbar_wait(&bar_tempty[buf], ((it / kNB) & 1) ^ 1, &abort_flag)) { ok = false; break; }
+        if (!mbar_wait_t<kConv>(&bar_tempty[buf], ((it / kNB) & 1) ^ 1, &abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * BN;
         if constexpr (kConv) {
           const int groups = p.num_kb / kbpg;
           int kb = 0;
           for (int g = 0; g < groups; ++g) {
-            ok &= mbar_wait(&bar_hfull[hs], hph, &abort_flag);
+            ok &= mbar_wait_t<kConv>(&bar_hfull[hs], hph, &abort_flag);
             tc_fence_after();
             const uint32_t halo_lo = (base_u32 + p.h_off + hs * p.conv.halo_bytes) >> 4;
             if (resident) {
@@ -807,7 +824,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
               ++kb;
             } else {
               for (int i = 0; i < kbpg; ++i, ++kb) {
-                ok &= mbar_wait(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag);
+                ok &= mbar_wait_t<kConv>(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag);
                 tc_fence_after();
                 const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(s) * b_step);
 #pragma unroll
@@ -823,7 +840,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
           }
         } else {
           for (int kb = 0; kb < p.num_kb; ++kb) {
-            ok &= mbar_wait(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag);
+            ok &= mbar_wait_t<kConv>(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag);
             tc_fence_after();
             const uint64_t a_desc0 = sw128_tmpl + (a_stage0 + uint32_t(s) * a_step);
             const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(s) * b_step);
@@ -854,6 +871,21 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
     k.qnf = float(p.epi.qn);
     k.qpf = float(p.epi.qp);
     k.relu_in_clamp = p.epi.out_kind == 3 && p.epi.qn >= 0 && p.epi.aux == nullptr;
+    // Conv: alpha / beta are copied into shared memory once; every 16-column
+    // chunk then reads them there instead of making a round trip to L2.
+    const float* sa = nullptr;
+    const float* sb = nullptr;
+    if (kConv && p.conv.ab_off) {
+      float* a_s = reinterpret_cast<float*>(base + p.conv.ab_off);
+      float* b_s = a_s + p.conv.ab_pitch;
+      for (int i = (warp - 4) * 32 + lane; i < p.epi.n_total; i += kEpiWarps * 32) {
+        if (p.epi.alpha) a_s[i] = p.epi.alpha[i];
+        if (p.epi.beta) b_s[i] = p.epi.beta[i];
+      }
+      bar_sync(8, kEpiWarps * 32);
+      sa = p.epi.alpha ? a_s : nullptr;
+      sb = p.epi.beta ? b_s : nullptr;
+    }
     int it = set;
     for (int t = blockIdx.x + set * gridDim.x; t < total_tiles; t += kNB * gridDim.x, it += kNB) {
       const int buf = set;
@@ -870,7 +902,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
         }
       }
       int ok = 1;
-      if (lane == 0) ok = mbar_wait(&bar_tfull[buf], (it / kNB) & 1, &abort_flag) ? 1 : 0;
+      if (lane == 0) ok = mbar_wait_idle(&bar_tfull[buf], (it / kNB) & 1, &abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         if (lane == 0) atomicOr(p.err, kErrTimeoutEpilogue);
@@ -897,7 +929,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
         tmem_ld_wait();
         if (valid) {
           const int n = nt * BN + c0;
-          epilogue16(p.epi, k, acc, n, out_off + (long long)n * p.epi.s_ch, prow);
+          epilogue16<kConv>(p.epi, k, acc, n, out_off + (long long)n * p.epi.s_ch, prow, sa, sb);
         }
       }
       tc_fence_before();
@@ -929,7 +961,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
     // the warp after the observed phase.
     auto wait_warp = [&](uint64_t* bar, uint32_t parity) -> bool {
       int got = 1;
-      if (lane == 0) got = mbar_wait(bar, parity, &abort_flag) ? 1 : 0;
+      if (lane == 0) got = mbar_wait_t<kConv>(bar, parity, &abort_flag) ? 1 : 0;
       got = __shfl_sync(0xffffffffu, got, 0);
       return got != 0;
     };

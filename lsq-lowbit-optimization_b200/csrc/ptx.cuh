@@ -82,11 +82,28 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
   return ok != 0;
 }
 
-// Wait part of mbar_wait, kept out of line: an inlined wait loop inside the
-// MMA issue loop slows that loop down even when it is never entered. Each
-// try suspends for at most 20 us; the abort flag and the time limit are
-// checked after every try.
+// Spin part of mbar_wait, kept out of line: an inlined spin loop inside the
+// MMA issue loop slows that loop down even when it is never entered.
 __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  const unsigned long long t0 = global_timer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++spins & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// Sleeping counterpart for long waits (an epilogue warp set waiting for its
+// next accumulator tile): each try suspends for at most 20 us, so the warp
+// takes no issue slots from the MMA thread and the busy epilogue warps; the
+// abort flag and the time limit are checked after every try.
+__device__ __noinline__ bool mbar_wait_idle_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   const unsigned long long t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
@@ -96,6 +113,18 @@ __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, vola
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_idle_slow(bar, parity, abort_flag);
+}
+
+// Sleeping (kIdle) or spinning wait, chosen per kernel.
+template <bool kIdle>
+__device__ __forceinline__ bool mbar_wait_t(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return kIdle ? mbar_wait_idle_slow(bar, parity, abort_flag) : mbar_wait_slow(bar, parity, abort_flag);
 }
 
 // Bounded wait for the phase with the given parity. Returns false (and sets
