@@ -154,6 +154,17 @@ void fill_epi(EpiParams& d, const w4a8_epilogue* e, void* out, int n_total) {
   d.aux = e->aux;
   d.aux_ld = e->aux_ld;
   d.n_total = n_total;
+  d.vec16 = 0;
+}
+
+// Sets vec16 once the output strides are known: the epilogue may then skip
+// its per-chunk shape and alignment checks.
+void set_vec16(EpiParams& d) {
+  auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  const long long esz = d.out_kind == 1 ? 4 : (d.out_kind == 2 ? 2 : 1);
+  d.vec16 = d.out_kind != 0 && d.s_ch == 1 && d.n_total % 16 == 0 && al(d.out) && (d.s_pix * esz) % 16 == 0 &&
+            (d.s_img * esz) % 16 == 0 && (!d.alpha || al(d.alpha)) && (!d.beta || al(d.beta)) &&
+            (!d.residual || (al(d.residual) && d.res_ld % 4 == 0)) && (!d.aux || (al(d.aux) && d.aux_ld % 4 == 0));
 }
 
 int pick_stages(uint32_t per_stage, uint32_t reserved) {
@@ -273,6 +284,7 @@ int gemm_w4(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int M, int
   p.epi.s_img = 0;
   p.epi.s_pix = ldc;
   p.epi.s_ch = 1;
+  set_vec16(p.epi);
 
   CUtensorMap tA, tW;
   {
@@ -451,6 +463,7 @@ extern "C" int w4a8_gemm(const int8_t* A, int64_t lda, const void* W, int64_t ld
   p.epi.s_img = 0;
   p.epi.s_pix = ldc;
   p.epi.s_ch = 1;
+  set_vec16(p.epi);
 
   CUtensorMap tA, tW, tH[4];
   std::memset(tH, 0, sizeof(tH));
@@ -666,6 +679,7 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
     p.epi.s_pix = 1;
     p.epi.s_ch = (long long)g->ho * g->wo;
   }
+  set_vec16(p.epi);
 
   CUtensorMap tA, tW, tH[4];
   std::memset(&tA, 0, sizeof(tA));

@@ -82,6 +82,8 @@ struct EpiParams {
   long long s_img, s_pix, s_ch;  // output element strides
   int n_total;                   // valid columns
   int acc_fits_22;               // host-proven |acc| < 2^22: no per-value range check
+  int vec16;                     // host-proven: every 16-column chunk below n_total is full and
+                                 // 16-byte aligned in out, alpha, beta, residual and aux
 };
 
 struct ConvParams {
@@ -323,6 +325,10 @@ template <bool kSmemAB = false>
 __device__ __forceinline__ void epilogue16(const EpiParams& e, const EpiConsts& k, const uint32_t* acc, int n,
                                            long long out_off, long long prow, const float* sa = nullptr,
                                            const float* sb = nullptr) {
+  if (e.vec16) {
+    if (n < e.n_total) epilogue16_fast<kSmemAB>(e, k, acc, n, out_off, prow, sa, sb);
+    return;
+  }
   const int ncols = min(16, e.n_total - n);
   if (ncols <= 0) return;
   const bool vec = (ncols == 16) && (e.s_ch == 1);
