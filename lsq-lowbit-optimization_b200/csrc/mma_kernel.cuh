@@ -810,33 +810,50 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
             ok &= mbar_wait_t<kConv>(&bar_hfull[hs], hph, &abort_flag);
             tc_fence_after();
             const uint32_t halo_lo = (base_u32 + p.h_off + hs * p.conv.halo_bytes) >> 4;
+            // A k-block's four step descriptors are loaded before its MMAs
+            // issue, and the next block's while they issue: the MMA asm's
+            // memory clobber would otherwise order each load after the
+            // previous MMA and expose its latency once per MMA.
+            const uint64_t* sd = p.conv.step_desc;
+            uint64_t dn0 = sd[0], dn1 = sd[1], dn2 = sd[2], dn3 = sd[3];
             if (resident) {
               // Resident weights: the zero-weight padding steps of the
               // group's last k-block are not issued.
               for (int i = 0; i < kbpg - 1; ++i, ++kb) {
+                const uint64_t d0 = dn0 + halo_lo, d1 = dn1 + halo_lo, d2 = dn2 + halo_lo, d3 = dn3 + halo_lo;
+                const uint64_t* nx = sd + 4 * (i + 1);
+                dn0 = nx[0];
+                dn1 = nx[1];
+                dn2 = nx[2];
+                dn3 = nx[3];
                 const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(kb) * b_step);
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                  mma_i8_ss(d_tmem, p.conv.step_desc[i * 4 + j] + halo_lo, b_desc0 + 2 * j, idesc,
-                            (kb | j) != 0 ? 1u : 0u);
+                mma_i8_ss(d_tmem, d0, b_desc0, idesc, kb != 0 ? 1u : 0u);
+                mma_i8_ss(d_tmem, d1, b_desc0 + 2, idesc, 1u);
+                mma_i8_ss(d_tmem, d2, b_desc0 + 4, idesc, 1u);
+                mma_i8_ss(d_tmem, d3, b_desc0 + 6, idesc, 1u);
               }
               const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(kb) * b_step);
-              const int i = kbpg - 1;
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                if (j < p.conv.tail_steps)
-                  mma_i8_ss(d_tmem, p.conv.step_desc[i * 4 + j] + halo_lo, b_desc0 + 2 * j, idesc,
-                            (kb | j) != 0 ? 1u : 0u);
+              const int tail = p.conv.tail_steps;
+              mma_i8_ss(d_tmem, dn0 + halo_lo, b_desc0, idesc, kb != 0 ? 1u : 0u);
+              if (tail > 1) mma_i8_ss(d_tmem, dn1 + halo_lo, b_desc0 + 2, idesc, 1u);
+              if (tail > 2) mma_i8_ss(d_tmem, dn2 + halo_lo, b_desc0 + 4, idesc, 1u);
+              if (tail > 3) mma_i8_ss(d_tmem, dn3 + halo_lo, b_desc0 + 6, idesc, 1u);
               ++kb;
             } else {
               for (int i = 0; i < kbpg; ++i, ++kb) {
+                const uint64_t d0 = dn0 + halo_lo, d1 = dn1 + halo_lo, d2 = dn2 + halo_lo, d3 = dn3 + halo_lo;
+                const uint64_t* nx = sd + 4 * min(i + 1, kbpg - 1);
+                dn0 = nx[0];
+                dn1 = nx[1];
+                dn2 = nx[2];
+                dn3 = nx[3];
                 ok &= mbar_wait_t<kConv>(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag);
                 tc_fence_after();
                 const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(s) * b_step);
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                  mma_i8_ss(d_tmem, p.conv.step_desc[i * 4 + j] + halo_lo, b_desc0 + 2 * j, idesc,
-                            (kb | j) != 0 ? 1u : 0u);
+                mma_i8_ss(d_tmem, d0, b_desc0, idesc, kb != 0 ? 1u : 0u);
+                mma_i8_ss(d_tmem, d1, b_desc0 + 2, idesc, 1u);
+                mma_i8_ss(d_tmem, d2, b_desc0 + 4, idesc, 1u);
+                mma_i8_ss(d_tmem, d3, b_desc0 + 6, idesc, 1u);
                 mma_commit(&bar_empty[s]);
                 if (++s == p.stages) { s = 0; ph ^= 1; }
               }
