@@ -75,10 +75,21 @@ class ClockSampler:
         try:
             self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
                  "-i", str(self.index)], stdout=self.tmp, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return self
+        # nvidia-smi takes a moment to start: the timed region (a few hundred ms at
+        # the default step count) begins only once the first sample is written.
+        t0 = time.time()
+        while time.time() - t0 < 5.0 and self.proc.poll() is None:
+            try:
+                if Path(self.tmp.name).read_text().count("\n") >= 1:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.02)
         return self
 
     def stop(self):
