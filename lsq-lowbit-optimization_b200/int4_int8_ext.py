@@ -252,6 +252,22 @@ def repack_oihw_int4(w_packed: torch.Tensor, c: int, kh: int, kw: int, c_pad: in
     return out
 
 
+# int8 weight bytes (O x kh x kw x padded C) above which a 4-bit conv's weights
+# cannot stay resident in the conv kernel's shared memory. Streamed 4-bit weights
+# would be re-expanded for every output tile, so callers expand them once
+# (expand_int4_rows) and pass int8 codes instead: same values, same int32 sums.
+CONV_STREAMED_W4_BYTES = 160 * 1024
+
+
+def expand_int4_rows(packed: torch.Tensor) -> torch.Tensor:
+    """Packed int4 rows [O, ldw] (low nibble = even element, two's complement)
+    -> int8 codes [O, 2 * ldw], row stride a multiple of 16 when ldw is."""
+    p = packed.to(torch.int16)
+    lo, hi = p & 0xF, (p >> 4) & 0xF
+    lo, hi = lo - ((lo & 8) << 1), hi - ((hi & 8) << 1)
+    return torch.stack((lo, hi), dim=-1).reshape(packed.shape[0], -1).to(torch.int8).contiguous()
+
+
 def conv_channels_padded(c: int, stride: int = 1) -> int:
     """Channel count the conv kernel accepts: 16 (stride 1 only), 32, 64 or
     a multiple of 128 — the halo stores one pixel per 16/32/64/128-byte

@@ -68,7 +68,7 @@ class Int4WeightInt8ActConv2d(nn.Module):
             self.bias = nn.Parameter(torch.zeros(self.out_channels, dtype=torch.float32))
         else:
             self.register_parameter("bias", None)
-        self._kernel_weight = None  # (key, tensor) in the conv kernel's order
+        self._kernel_weight = None  # (key, tensor, kind) in the conv kernel's order
         self._alpha_cache = None
 
     @torch.no_grad()
@@ -99,14 +99,20 @@ class Int4WeightInt8ActConv2d(nn.Module):
                 and self.padding[0] == self.padding[1]
                 and kh * kw * min(ext.conv_channels_padded(self.in_channels, self.stride[0]), 128) <= 2048)
 
-    def _conv_weight(self) -> torch.Tensor:
+    def _conv_weight(self):
+        """(weights in the conv kernel's order, weight kind). Weights too large
+        to stay resident in the kernel's shared memory are kept as int8 codes
+        (ext.CONV_STREAMED_W4_BYTES), expanded once per weight version."""
         wp = self.weight_packed
         key = (wp.data_ptr(), wp._version, wp.device)
         if self._kernel_weight is None or self._kernel_weight[0] != key:
             kh, kw = self.kernel_size
             cp = ext.conv_channels_padded(self.in_channels, self.stride[0])
-            self._kernel_weight = (key, ext.repack_oihw_int4(wp.contiguous(), self.in_channels, kh, kw, cp))
-        return self._kernel_weight[1]
+            w, kind = ext.repack_oihw_int4(wp.contiguous(), self.in_channels, kh, kw, cp), ext.W_INT4
+            if self.out_channels * kh * kw * cp > ext.CONV_STREAMED_W4_BYTES:
+                w, kind = ext.expand_int4_rows(w), ext.W_INT8
+            self._kernel_weight = (key, w, kind)
+        return self._kernel_weight[1], self._kernel_weight[2]
 
     def _alpha(self, device):
         """Scalar alpha (float) or per-channel alpha tensor. The reference's
@@ -135,7 +141,8 @@ class Int4WeightInt8ActConv2d(nn.Module):
             kh, kw = self.kernel_size
             # Padding of the fused 3x3 op quantises 0.0 (csrc/int4_int8_kernels.cu:242-250);
             # the unfold path pads the codes with 0 (int4_conv2d.py:172-181).
-            return ext.conv_nchw(x, self._conv_weight(), ext.W_INT4, self.in_channels, kh, kw, self.stride[0],
+            w, kind = self._conv_weight()
+            return ext.conv_nchw(x, w, kind, self.in_channels, kh, kw, self.stride[0],
                                  self.padding[0], self.a_scale_host, self.a_qn, self.a_qp, alpha_scalar=alpha_s,
                                  alpha=alpha_t, bias=self.bias, out_dtype=self.out_dtype,
                                  pad_code_of_zero=self.is_spatial_3x3)

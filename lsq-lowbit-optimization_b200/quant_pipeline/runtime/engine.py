@@ -91,11 +91,6 @@ def conv_spec(layer: nn.Module, bn: Optional[nn.BatchNorm2d]) -> ConvSpec:
     return ConvSpec(w, bits, stride, pad, qin, alpha, beta)
 
 
-# int8 weight bytes above which a 4-bit conv streams its weights instead of
-# keeping them resident in shared memory (ResNet-18: the 3x3 convs of layers 3-4).
-STREAMED_W4_BYTES = 160 * 1024
-
-
 def _kernel_weights(w_ohwi: torch.Tensor, bits: int, c_pad: int, device) -> torch.Tensor:
     """OHWI codes -> device weights in the conv kernel's order (channel
     groups of 128 outermost when c_pad > 128), row stride a multiple of 16."""
@@ -214,12 +209,13 @@ class W4A8ResNetEngine:
         ops = 2.0 * pix * (macs_per_pixel if macs_per_pixel is not None else o * kh * kw * c)
         nbytes = n * h * w * c + opix * o * out.element_size() + o * kh * kw * c * spec.w_bits / 8
         nbytes += (opix * o * 4 if residual is not None else 0) + (opix * o * 4 if aux is not None else 0)
-        # 4-bit weights whose int8 form exceeds STREAMED_W4_BYTES cannot stay
-        # resident in shared memory: the conv kernel would re-expand the same
-        # nibbles for every output tile. They are expanded once here and
-        # streamed as int8 codes (same values, same int32 sums).
+        # 4-bit weights whose int8 form exceeds ext.CONV_STREAMED_W4_BYTES
+        # cannot stay resident in shared memory (ResNet-18: the 3x3 convs of
+        # layers 3-4): the conv kernel would re-expand the same nibbles for
+        # every output tile. They are expanded once here and streamed as int8
+        # codes (same values, same int32 sums).
         bits = spec.w_bits
-        if bits == 4 and o * kh * kw * c > STREAMED_W4_BYTES:
+        if bits == 4 and o * kh * kw * c > ext.CONV_STREAMED_W4_BYTES:
             bits = 8
         wk = _kernel_weights(spec.w_codes, bits, c, self.device)
         alpha = spec.alpha.to(self.device)

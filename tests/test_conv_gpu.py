@@ -113,6 +113,34 @@ def test_module_matches_reference_golden(cuda):
         assert_equal(y, d[f"{name}_y"], f"module {name} vs reference")
 
 
+def test_module_large_weights_stream_int8(cuda):
+    """A conv whose int8 weights exceed CONV_STREAMED_W4_BYTES runs on int8
+    codes expanded once from its packed int4 weights; outputs equal the
+    4-bit-weight kernel path bit for bit."""
+    from quant_pipeline.ops import Int4WeightInt8ActConv2d
+
+    g = rng(43)
+    cin = cout = 256
+    m = Int4WeightInt8ActConv2d(cin, cout, (3, 3), (1, 1), (1, 1), (1, 1), 1, 0.0123, 0.05, -128, 127,
+                                out_dtype=torch.float32, bias=True)
+    m.load_int4_weight(torch.from_numpy(g.integers(-8, 8, (cout, cin, 3, 3)).astype(np.int8)))
+    with torch.no_grad():
+        m.bias.copy_(torch.from_numpy(g.normal(0, 0.1, cout).astype(np.float32)))
+    m = m.to(cuda)
+    assert cout * 9 * cin > ext.CONV_STREAMED_W4_BYTES
+    w8, kind = m._conv_weight()
+    assert kind == ext.W_INT8 and w8.dtype == torch.int8
+    x = to_dev(g.normal(0, 2, (2, cin, 7, 9)).astype(np.float32), cuda)
+    with torch.no_grad():
+        y = m(x)
+    w4 = ext.repack_oihw_int4(m.weight_packed.contiguous(), cin, 3, 3, cin)
+    alpha_s, alpha_t = m._alpha(x.device)
+    want = ext.conv_nchw(x, w4, ext.W_INT4, cin, 3, 3, 1, 1, m.a_scale_host, m.a_qn, m.a_qp, alpha_scalar=alpha_s,
+                         alpha=alpha_t, bias=m.bias, out_dtype=torch.float32, pad_code_of_zero=m.is_spatial_3x3)
+    torch.cuda.synchronize()
+    assert torch.equal(y, want)
+
+
 def test_s2d_quantize_matches_oracle(cuda):
     """fp32 NCHW images -> int8 space-to-depth codes (channel (dy*2+dx)*3+c,
     padded to 16): clamp(rint(x / s)) in IEEE float32, checked on values at

@@ -46,6 +46,17 @@ def test_kernel_weight_order_groups_of_128():
     assert got.shape[1] % 16 == 0
 
 
+def test_expand_int4_rows_matches_oracle_packing():
+    """Packed int4 rows -> int8 codes (the int8 form large-weight convs stream)."""
+    import int4_int8_ext as ext
+    g = np.random.default_rng(41)
+    w = g.integers(-8, 8, (37, 96), dtype=np.int8)
+    packed = torch.from_numpy(orc.pack_int4(w))
+    got = ext.expand_int4_rows(packed)
+    assert got.dtype == torch.int8 and tuple(got.shape) == (37, 96)
+    assert np.array_equal(got.numpy(), w)
+
+
 def test_c_abi_exports_every_declared_symbol():
     import build_native
     import int4_int8_ext as ext
