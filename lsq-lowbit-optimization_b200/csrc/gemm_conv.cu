@@ -155,6 +155,7 @@ void fill_epi(EpiParams& d, const w4a8_epilogue* e, void* out, int n_total) {
   d.aux_ld = e->aux_ld;
   d.n_total = n_total;
   d.vec16 = 0;
+  d.v8 = 0;
 }
 
 // Sets vec16 once the output strides are known: the epilogue may then skip
@@ -165,6 +166,11 @@ void set_vec16(EpiParams& d) {
   d.vec16 = d.out_kind != 0 && d.s_ch == 1 && d.n_total % 16 == 0 && al(d.out) && (d.s_pix * esz) % 16 == 0 &&
             (d.s_img * esz) % 16 == 0 && (!d.alpha || al(d.alpha)) && (!d.beta || al(d.beta)) &&
             (!d.residual || (al(d.residual) && d.res_ld % 4 == 0)) && (!d.aux || (al(d.aux) && d.aux_ld % 4 == 0));
+  // 256-bit float32 accesses: 32-byte aligned bases and strides of 8 floats.
+  auto al32 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 31) == 0; };
+  d.v8 = d.vec16 && (!d.residual || (al32(d.residual) && d.res_ld % 8 == 0)) &&
+         (!d.aux || (al32(d.aux) && d.aux_ld % 8 == 0)) &&
+         (d.out_kind != 1 || (al32(d.out) && d.s_pix % 8 == 0 && d.s_img % 8 == 0));
 }
 
 int pick_stages(uint32_t per_stage, uint32_t reserved) {

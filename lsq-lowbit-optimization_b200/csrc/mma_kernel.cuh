@@ -84,7 +84,17 @@ struct EpiParams {
   int acc_fits_22;               // host-proven |acc| < 2^22: no per-value range check
   int vec16;                     // host-proven: every 16-column chunk below n_total is full and
                                  // 16-byte aligned in out, alpha, beta, residual and aux
+  int v8;                        // host-proven (with vec16): the float32 residual, aux and float32
+                                 // out chunks are 32-byte aligned (256-bit accesses)
 };
+
+// 32-byte global accesses (four float pairs).
+__device__ __forceinline__ void ldg256(const float* p, uint64_t& a, uint64_t& b, uint64_t& c, uint64_t& d) {
+  asm volatile("ld.global.v4.u64 {%0, %1, %2, %3}, [%4];" : "=l"(a), "=l"(b), "=l"(c), "=l"(d) : "l"(p));
+}
+__device__ __forceinline__ void stg256(float* p, uint64_t a, uint64_t b, uint64_t c, uint64_t d) {
+  asm volatile("st.global.v4.u64 [%0], {%1, %2, %3, %4};" ::"l"(p), "l"(a), "l"(b), "l"(c), "l"(d) : "memory");
+}
 
 struct ConvParams {
   int ho, wo;              // output size
@@ -248,12 +258,21 @@ __device__ __forceinline__ void epilogue16_fast(const EpiParams& e, const EpiCon
     }
   }
   if (e.residual) {
-    const ulonglong2* r2 = reinterpret_cast<const ulonglong2*>(e.residual + prow * e.res_ld + n);
+    const float* rp = e.residual + prow * e.res_ld + n;
+    if (e.v8) {
+      uint64_t r[8];
+      ldg256(rp, r[0], r[1], r[2], r[3]);
+      ldg256(rp + 8, r[4], r[5], r[6], r[7]);
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const ulonglong2 v = r2[g];
-      y[2 * g] = add2(y[2 * g], v.x);
-      y[2 * g + 1] = add2(y[2 * g + 1], v.y);
+      for (int j = 0; j < 8; ++j) y[j] = add2(y[j], r[j]);
+    } else {
+      const ulonglong2* r2 = reinterpret_cast<const ulonglong2*>(rp);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const ulonglong2 v = r2[g];
+        y[2 * g] = add2(y[2 * g], v.x);
+        y[2 * g + 1] = add2(y[2 * g + 1], v.y);
+      }
     }
   }
   if (e.relu && !k.relu_in_clamp) {
@@ -261,14 +280,26 @@ __device__ __forceinline__ void epilogue16_fast(const EpiParams& e, const EpiCon
     for (int j = 0; j < 8; ++j) y[j] = fpair(fmaxf(flo(y[j]), 0.0f), fmaxf(fhi(y[j]), 0.0f));
   }
   if (e.aux) {
-    ulonglong2* d2 = reinterpret_cast<ulonglong2*>(e.aux + prow * e.aux_ld + n);
+    float* ap = e.aux + prow * e.aux_ld + n;
+    if (e.v8) {
+      stg256(ap, y[0], y[1], y[2], y[3]);
+      stg256(ap + 8, y[4], y[5], y[6], y[7]);
+    } else {
+      ulonglong2* d2 = reinterpret_cast<ulonglong2*>(ap);
 #pragma unroll
-    for (int g = 0; g < 4; ++g) d2[g] = make_ulonglong2(y[2 * g], y[2 * g + 1]);
+      for (int g = 0; g < 4; ++g) d2[g] = make_ulonglong2(y[2 * g], y[2 * g + 1]);
+    }
   }
   if (e.out_kind == 1) {
-    ulonglong2* d2 = reinterpret_cast<ulonglong2*>(static_cast<float*>(e.out) + out_off);
+    float* op = static_cast<float*>(e.out) + out_off;
+    if (e.v8) {
+      stg256(op, y[0], y[1], y[2], y[3]);
+      stg256(op + 8, y[4], y[5], y[6], y[7]);
+    } else {
+      ulonglong2* d2 = reinterpret_cast<ulonglong2*>(op);
 #pragma unroll
-    for (int g = 0; g < 4; ++g) d2[g] = make_ulonglong2(y[2 * g], y[2 * g + 1]);
+      for (int g = 0; g < 4; ++g) d2[g] = make_ulonglong2(y[2 * g], y[2 * g + 1]);
+    }
     return;
   }
   if (e.out_kind == 2) {
