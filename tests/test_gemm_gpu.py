@@ -102,6 +102,38 @@ def test_epilogue_residual_relu_aux(cuda):
     assert_equal(out, q, "requant")
 
 
+@pytest.mark.parametrize("pad", [4, 8])
+def test_epilogue_padded_float_rows(cuda, pad):
+    """Residual, float side output and float32 output with row strides of
+    n + pad floats: pad 4 keeps rows 16-byte but not 32-byte aligned (the
+    16-byte vector path), pad 8 keeps 32-byte rows (the 32-byte path)."""
+    g = rng(6 + pad)
+    m, n, k = 136, 160, 256
+    x = rand_i8(g, (m, k), 0, 127)
+    w = rand_i4(g, (n, k))
+    alpha = g.uniform(1e-4, 1e-3, n).astype(np.float32)
+    beta = g.normal(0, 0.1, n).astype(np.float32)
+    res = np.zeros((m, n + pad), np.float32)
+    res[:, :n] = g.normal(0, 1.0, (m, n))
+    bp = orc.pack_int4(w)
+    y = orc.epilogue(orc.int4_int8_gemm(x, bp), alpha, beta, res[:, :n], relu=True)
+    aux = torch.full((m, n + pad), float("nan"), dtype=torch.float32, device=cuda)
+    out = torch.empty((m, n), dtype=torch.int8, device=cuda)
+    epi = ext.make_epilogue(ext.OUT_S8, alpha=to_dev(alpha, cuda), beta=to_dev(beta, cuda),
+                            residual=to_dev(res, cuda), res_ld=n + pad, relu=True, out_scale=0.05, qn=0, qp=127,
+                            aux=aux, aux_ld=n + pad)
+    ext.gemm(to_dev(x, cuda), to_dev(bp, cuda), ext.W_INT4, k, epi, out)
+    assert_equal(aux[:, :n], y, "aux")
+    assert torch.isnan(aux[:, n:]).all(), "aux padding written"
+    assert_equal(out, orc.quantize(y, 0.05, 0, 127), "requant")
+    yf = torch.full((m, n + pad), float("nan"), dtype=torch.float32, device=cuda)
+    epi = ext.make_epilogue(ext.OUT_F32, alpha=to_dev(alpha, cuda), beta=to_dev(beta, cuda),
+                            residual=to_dev(res, cuda), res_ld=n + pad, relu=True)
+    ext.gemm(to_dev(x, cuda), to_dev(bp, cuda), ext.W_INT4, k, epi, yf[:, :n])
+    assert_equal(yf[:, :n], y, "f32 out")
+    assert torch.isnan(yf[:, n:]).all(), "out padding written"
+
+
 def test_linear_op_matches_oracle(cuda):
     g = rng(11)
     m, k, o = 37, 200, 96
