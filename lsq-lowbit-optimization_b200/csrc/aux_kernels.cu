@@ -249,7 +249,10 @@ __global__ void avgpool_q_kernel(const float* __restrict__ x, int8_t* __restrict
     const int img = int(i / c);
     const float* xi = x + (long long)img * hw * c + ch;
     float s = 0.0f;
-    for (int p = 0; p < hw; ++p) s = __fadd_rn(s, xi[(long long)p * c]);
+    // Unrolled so that several pixels' loads are in flight; the adds keep
+    // their order (pixel 0, 1, 2, ...).
+#pragma unroll 8
+    for (int p = 0; p < hw; ++p) s = __fadd_rn(s, __ldg(xi + (long long)p * c));
     const float mean = __fdiv_rn(s, float(hw));
     q[(long long)img * ldq + ch] = int8_t(quant1(mean, scale, qn, qp));
   }
