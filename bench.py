@@ -134,18 +134,57 @@ def time_events(fn, iters: int, warmup: int = 2) -> float:
 
 def cpu_oracle_rate(model, images: int, seed: int = 7) -> dict:
     """Images/s of the CPU oracle (numpy integer port) on this host."""
-    import numpy as np
     from oracle import resnet_oracle as ro
     from quant_pipeline.runtime.lsq_resnet import synthetic_images
 
     x = synthetic_images(images, seed=seed).numpy()
     t0 = time.perf_counter()
-    for i in range(images):
-        ro.resnet_forward(model, x[i:i + 1])
+    ro.resnet_forward(model, x)
     dt = time.perf_counter() - t0
     return {"value": images / dt, "unit": "images/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{images} images, one at a time, numpy integer oracle (float64 BLAS, "
+            "sample": f"{images} images per call, numpy integer oracle (exact float32/float64 BLAS, "
                       f"{os.cpu_count()} host threads)", "seconds": round(dt, 2)}
+
+
+def cpu_fakequant_rate(model, images: int, seed: int = 7) -> dict:
+    """The reference's CPU path for the whole network: the LSQ fake-quant
+    float32 forward (clamp(round(x/s))*s on activations and weights, float
+    conv / linear, BatchNorm, ReLU, pooling in torch) on the host cores,
+    after one warm-up call."""
+    from quant_pipeline.runtime.lsq_resnet import synthetic_images
+
+    torch.set_num_threads(os.cpu_count())
+    x = synthetic_images(images, seed=seed)
+    with torch.no_grad():
+        model(x[:2])
+        t0 = time.perf_counter()
+        model(x)
+        dt = time.perf_counter() - t0
+    return {"value": images / dt, "unit": "images/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"one batch of {images} images: LSQ fake-quant float32 forward in torch on the host "
+                      f"(the LSQ native model of the reference's flow), {torch.get_num_threads()} threads",
+            "seconds": round(dt, 2)}
+
+
+def cpu_baseline_leg(model, images: torch.Tensor, logits: torch.Tensor) -> tuple:
+    """The CPU leg: times the reference's CPU path (LSQ fake-quant forward)
+    on a bounded sample, and checks the engine's logits for the whole timed
+    batch against the integer oracle (the checker; exact by construction).
+    Returns (cpu_baseline, parity)."""
+    import numpy as np
+    from oracle import resnet_oracle as ro
+
+    base = cpu_fakequant_rate(model, int(images.shape[0]))
+    t0 = time.perf_counter()
+    want = ro.resnet_forward(model, images.numpy())
+    dt = time.perf_counter() - t0
+    got = logits.cpu().numpy()
+    parity = {"images": int(got.shape[0]), "checker": "CPU integer oracle (oracle/resnet_oracle.py)",
+              "bit_exact": bool(np.array_equal(got, want)), "rel_err": float(ro.rel_err(got, want)),
+              "top1_agreement": float(ro.top1_agreement(got, want)), "gate": "rel_err <= 1e-3, top-1 >= 0.999"}
+    parity["pass"] = parity["rel_err"] <= 1e-3 and parity["top1_agreement"] >= 0.999
+    base["oracle_port_images_per_s"] = round(got.shape[0] / dt, 2)
+    return base, parity
 
 
 def run_reference(args, rank: int) -> None:
@@ -155,7 +194,7 @@ def run_reference(args, rank: int) -> None:
 
     torch.set_num_threads(os.cpu_count())
     model = build_lsq_resnet(args.arch, seed=0)
-    per_step = 1 if args.steps + args.warmup > 50 else 4
+    per_step = 2 if args.steps + args.warmup > 50 else 8
     for _ in range(args.warmup):
         cpu_oracle_rate(model, per_step)
     t0 = time.perf_counter()
@@ -170,7 +209,7 @@ def run_reference(args, rank: int) -> None:
         "config": {"workload": WORKLOAD, "batch_per_step": per_step, "arch": args.arch,
                    "note": "CPU oracle (numpy port of the reference's integer path), bounded sample per step"},
         "cpu_baseline": {"value": value, "unit": "images/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": f"{per_step} image(s) per step x {args.steps} steps"},
+                         "sample": f"{per_step} images per step x {args.steps} steps"},
         "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -269,6 +308,139 @@ def fc_cfg0(device, hbm_gbs: float) -> dict:
     return {"shape_mnk": [256, 1000, 512], "us": round(ms * 1e3, 2), "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
             "hbm_frac": round(nbytes / (ms * 1e-3) / 1e9 / hbm_gbs, 4),
             "timing": "CUDA-graph replay of 20 calls; 1.4 MB of work, inputs L2-resident across calls"}
+
+
+def gemm_sweep(device, int8_peak: float, hbm_gbs: float) -> list:
+    """Config 1: W4A8 GEMM (int32 out) over M in {1, 32, 256, 4096} x N = K in
+    {1024, 4096, 8192}, per call with CUDA events after a read-only 256 MiB
+    L2 flush; TOPS against the int8 peak and GB/s against HBM."""
+    import int4_int8_ext as ext
+
+    gen = torch.Generator(device=device).manual_seed(3)
+    flush = torch.ones(256 << 20, dtype=torch.uint8, device=device)
+    out = []
+    for nk in (1024, 4096, 8192):
+        w = torch.randint(0, 256, (nk, nk // 2), dtype=torch.uint8, device=device, generator=gen)
+        for m in (1, 32, 256, 4096):
+            a = torch.randint(-128, 128, (m, nk), dtype=torch.int8, device=device, generator=gen)
+            c = torch.empty((m, nk), dtype=torch.int32, device=device)
+            epi = ext.make_epilogue(ext.OUT_S32)
+            for _ in range(3):
+                ext.gemm(a, w, ext.W_INT4, nk, epi, c)
+            total, iters = 0.0, 10
+            for _ in range(iters):
+                flush.max()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                ext.gemm(a, w, ext.W_INT4, nk, epi, c)
+                e1.record()
+                torch.cuda.synchronize()
+                total += e0.elapsed_time(e1)
+            ms = total / iters
+            tops = 2.0 * m * nk * nk / (ms * 1e-3) / 1e12
+            gbs = (a.numel() + w.numel() + c.numel() * 4) / (ms * 1e-3) / 1e9
+            out.append({"mnk": [m, nk, nk], "us": round(ms * 1e3, 2), "tops": round(tops, 1),
+                        "tensor_frac": round(tops / int8_peak, 4), "gbs": round(gbs, 1),
+                        "hbm_frac": round(gbs / hbm_gbs, 4)})
+    return out
+
+
+def conv_cfg2(device, int8_peak: float, hbm_gbs: float) -> list:
+    """Config 2 at full size: NHWC int8 [256, 56, 56, 64] post-ReLU codes, int4
+    weights, per-channel weight scale, bias, ReLU and int8 requant (scale
+    0.05) fused; the stride-2 64->128 variant and its 1x1 stride-2 shortcut
+    (float32 identity out). Per launch with CUDA events (inputs and outputs
+    exceed L2 together)."""
+    import int4_int8_ext as ext
+
+    gen = torch.Generator(device=device).manual_seed(4)
+    n, h, w, c = 256, 56, 56, 64
+    x = torch.randint(0, 128, (n, h, w, c), dtype=torch.int8, device=device, generator=gen)
+    out = []
+    for name, o, k, s, pad, kind in (("3x3s1", 64, 3, 1, 1, ext.OUT_S8), ("3x3s2", 128, 3, 2, 1, ext.OUT_S8),
+                                     ("1x1s2", 128, 1, 2, 0, ext.OUT_F32)):
+        ho = (h + 2 * pad - k) // s + 1
+        wt = torch.randint(0, 256, (o, (k * k * c) // 2), dtype=torch.uint8, device=device, generator=gen)
+        alpha = torch.rand(o, device=device, generator=gen) * 9e-3 * 0.05 + 1e-3 * 0.05
+        bias = torch.randn(o, device=device, generator=gen) * 0.01
+        y = torch.empty((n, ho, ho, o), dtype=torch.int8 if kind == ext.OUT_S8 else torch.float32, device=device)
+        epi = (ext.make_epilogue(kind, alpha=alpha, beta=bias, relu=True, out_scale=0.05, qn=0, qp=127)
+               if kind == ext.OUT_S8 else ext.make_epilogue(kind, alpha=alpha, beta=bias))
+        geom = ext.ConvGeom(n, h, w, c, k, k, s, pad, pad, ho, ho, o, ext.LAYOUT_NHWC, o)
+        ms = time_events(lambda: ext.conv2d_nhwc(x, wt, ext.W_INT4, geom, epi, y), iters=20, warmup=3)
+        ops = 2.0 * n * ho * ho * o * c * k * k
+        nbytes = x.numel() + y.numel() * y.element_size() + wt.numel() + 8 * o
+        tops, gbs = ops / (ms * 1e-3) / 1e12, nbytes / (ms * 1e-3) / 1e9
+        out.append({"conv": name, "ms": round(ms, 4), "tops": round(tops, 1),
+                    "tensor_frac": round(tops / int8_peak, 4), "gbs": round(gbs, 1),
+                    "hbm_frac": round(gbs / hbm_gbs, 4)})
+    return out
+
+
+def cpu_cfg012() -> dict:
+    """The reference's CPU integer path for configs 0-2, timed on the host
+    cores with torch: its own check pattern A.int32 @ unpack(Bp).int32.T
+    (benchmarks/benchmark_inference.py:67-76) for the fc layer and a GEMM
+    sample, and quantised unfold + the same int32 matmul for the conv
+    (quant_pipeline/ops/int4_conv2d.py:171-191), on bounded samples."""
+    import torch.nn.functional as F
+    from quant_pipeline.quantization.int4_pack import unpack_int4_weights
+
+    torch.set_num_threads(os.cpu_count())
+    gen = torch.Generator().manual_seed(5)
+
+    def best(fn, reps=3):
+        fn()
+        t = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            t.append(time.perf_counter() - t0)
+        return min(t)
+
+    res = {"cores": torch.get_num_threads()}
+    x = torch.randint(-128, 128, (256, 512), dtype=torch.int8, generator=gen)
+    wp = torch.randint(0, 256, (1000, 256), dtype=torch.uint8, generator=gen)
+    dt = best(lambda: x.to(torch.int32) @ unpack_int4_weights(wp).to(torch.int32).t())
+    res["cfg0_fc"] = {"mnk": [256, 1000, 512], "us": round(dt * 1e6, 1), "gops": round(2 * 256 * 1000 * 512 / dt / 1e9, 2)}
+    m, nk = 32, 4096
+    a = torch.randint(-128, 128, (m, nk), dtype=torch.int8, generator=gen)
+    wp = torch.randint(0, 256, (nk, nk // 2), dtype=torch.uint8, generator=gen)
+    dt = best(lambda: a.to(torch.int32) @ unpack_int4_weights(wp).to(torch.int32).t())
+    res["cfg1_gemm_sample"] = {"mnk": [m, nk, nk], "us": round(dt * 1e6, 1), "gops": round(2 * m * nk * nk / dt / 1e9, 2)}
+    imgs = 4
+    xq = torch.randint(0, 128, (imgs, 64, 56, 56), dtype=torch.int8, generator=gen)
+    wq = torch.randint(0, 256, (64, 288), dtype=torch.uint8, generator=gen)
+
+    def conv():
+        cols = F.unfold(xq.to(torch.float32), 3, padding=1).transpose(1, 2).reshape(-1, 576).to(torch.int32)
+        return cols @ unpack_int4_weights(wq).to(torch.int32).t()
+
+    dt = best(conv, reps=2)
+    res["cfg2_conv3x3_sample"] = {"images": imgs, "shape": "[n,56,56,64] 3x3 s1 64->64", "ms": round(dt * 1e3, 1),
+                                  "images_per_s": round(imgs / dt, 2),
+                                  "gops": round(2 * imgs * 56 * 56 * 64 * 576 / dt / 1e9, 2)}
+    res["note"] = "reported CPU baselines (unpacked int32 torch matmul, not BLAS), not optimisation targets"
+    return res
+
+
+def resnet50_rate(device, batch: int) -> dict:
+    """Config 4 on one GPU: the LSQ-converted ResNet-50 W4A8 engine at the
+    per-GPU batch (CUDA-graph replay, CUDA events), beside the FP16 cuDNN
+    torchvision ResNet-50."""
+    from quant_pipeline.runtime.engine import W4A8ResNetEngine
+    from quant_pipeline.runtime.lsq_resnet import build_lsq_resnet, synthetic_images
+
+    model = build_lsq_resnet("resnet50", seed=0)
+    eng = W4A8ResNetEngine(model, batch, device=device, use_graph=True)
+    eng.forward(synthetic_images(batch, seed=1).to(device))
+    ms = time_events(lambda: eng.forward(), iters=30, warmup=5)
+    launches = eng.launches
+    eng.release()
+    fp16 = fp16_cudnn_rate(device, batch, "resnet50")
+    return {"value": batch / (ms * 1e-3), "unit": "images/s", "ms_per_batch": round(ms, 4), "batch": batch,
+            "launches_per_batch": launches, "fp16_cudnn": round(fp16["value"], 1),
+            "w4a8_speedup": round(batch / (ms * 1e-3) / fp16["value"], 3)}
 
 
 def fp16_cudnn_rate(device, batch: int, arch: str) -> dict:
@@ -432,8 +604,16 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             fp16 = fp16_cudnn_rate(device, B, args.arch)
             fp16["w4a8_speedup"] = round(value / fp16["value"], 3)
             line["fp16_cudnn"] = fp16
-            torch.set_num_threads(os.cpu_count())
-            line["cpu_baseline"] = cpu_oracle_rate(model, 24)
+            line["gemm_sweep_cfg1"] = gemm_sweep(device, int8_peak, peaks["hbm_gbs"])
+            line["conv_cfg2"] = conv_cfg2(device, int8_peak, peaks["hbm_gbs"])
+            if args.arch == "resnet18":
+                line["resnet50_cfg4"] = resnet50_rate(device, B)
+            # The CPU leg: the reference's CPU path on the host cores, and the
+            # engine's logits for the timed batch checked against the oracle.
+            engine.forward(dev_images)
+            torch.cuda.synchronize()
+            line["cpu_baseline"], line["parity"] = cpu_baseline_leg(model, host_images, engine.logits)
+            line["cpu_baselines_cfg012"] = cpu_cfg012()
     engine.release()
     if line is not None:
         print(json.dumps(line), flush=True)

@@ -130,9 +130,11 @@ W4A8_API int w4a8_gemm_splitk_workspace(int M, int N, int K, int w_kind, size_t*
  * go to one fixed array of W4A8_NOALLOC_SCRATCH_BYTES (4 MiB) inside the
  * library. Every GPU that loads the library holds that array until the
  * process exits.
- * - INT4 weights only. Shapes with M * N * 4 above
+ * - INT4 weights only. Shapes that take no split (few-token GEMV, or
+ *   enough output tiles to fill the GPU) never touch the array and run as
+ *   w4a8_gemm at any size. Split-K shapes with M * N * 4 above
  *   W4A8_NOALLOC_SCRATCH_BYTES are rejected with W4A8_ERR_ARG and nothing
- *   is launched.
+ *   is launched (w4a8_gemm_splitk_workspace reports whether a shape splits).
  * - Results equal w4a8_gemm.
  * - The first call on a device looks up the array's device address (once per
  *   device, with that device current). Make that first call before any

@@ -12,13 +12,13 @@ namespace w4a8 {
 __device__ unsigned g_device_error;
 
 unsigned* device_error_word() {
-  static unsigned* cached[64] = {nullptr};
+  static PerDevice<unsigned*> cached;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  if (unsigned* c = cached.get(dev)) return c;
   void* ptr = nullptr;
   if (cudaGetSymbolAddress(&ptr, g_device_error) != cudaSuccess) return nullptr;
-  if (dev >= 0 && dev < 64) cached[dev] = static_cast<unsigned*>(ptr);
+  cached.set(dev, static_cast<unsigned*>(ptr));
   return static_cast<unsigned*>(ptr);
 }
 
@@ -31,13 +31,13 @@ template <int BN, bool I4, bool CV>
 int launch_t(const CUtensorMap& tA, const CUtensorMap& tW, const CUtensorMap* tH, const KParams& p, int grid,
              cudaStream_t st) {
   auto kern = w4a8_mma_kernel<BN, I4, CV>;
-  static bool attr_done[64] = {false};
+  static PerDevice<bool> attr_done;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+  if (!attr_done.get(dev)) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAttr) != cudaSuccess)
       return W4A8_ERR_LAUNCH;
-    if (dev >= 0 && dev < 64) attr_done[dev] = true;
+    attr_done.set(dev, true);
   }
   kern<<<grid, Roles<CV>::kThreads, kSmemAttr, st>>>(tA, tW, tH[0], tH[1], tH[2], tH[3], p);
   return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH;
@@ -46,13 +46,13 @@ int launch_t(const CUtensorMap& tA, const CUtensorMap& tW, const CUtensorMap* tH
 template <int BN, int CTA, bool SWAP>
 int launch_w4_t(const CUtensorMap& tA, const CUtensorMap& tW, const KParams& p, int grid, cudaStream_t st) {
   auto kern = w4a8_gemm_w4_kernel<BN, CTA, SWAP>;
-  static bool attr_done[64] = {false};
+  static PerDevice<bool> attr_done;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+  if (!attr_done.get(dev)) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAttr) != cudaSuccess)
       return W4A8_ERR_LAUNCH;
-    if (dev >= 0 && dev < 64) attr_done[dev] = true;
+    attr_done.set(dev, true);
   }
   cudaLaunchConfig_t cfg;
   std::memset(&cfg, 0, sizeof(cfg));
@@ -97,16 +97,16 @@ int launch_w4(int bn, int cta, bool swap, const CUtensorMap& tA, const CUtensorM
 
 // Co-resident CTA pairs of the pair W4 GEMM on the current device (cached).
 int pair_slots() {
-  static int cached[64] = {0};
+  static PerDevice<int> cached;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  if (const int c = cached.get(dev)) return c;
   CUtensorMap dummy;
   std::memset(&dummy, 0, sizeof(dummy));
   KParams p;
   std::memset(&p, 0, sizeof(p));
   const int n = launch_w4(256, 2, false, dummy, dummy, p, -1, nullptr);
-  if (n > 0 && dev >= 0 && dev < 64) cached[dev] = n;
+  if (n > 0) cached.set(dev, n);
   return n > 0 ? n : 0;
 }
 
@@ -395,15 +395,14 @@ static __device__ __align__(256) int g_splitk_scratch[W4A8_NOALLOC_SCRATCH_BYTES
 // Device address of g_splitk_scratch on the current device, looked up on the
 // first call per device (cudaGetSymbolAddress, return code checked) and cached.
 int* noalloc_scratch() {
-  static int* cached[64] = {nullptr};
+  static PerDevice<int*> cached;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!cached[dev]) {
-    void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_splitk_scratch) != cudaSuccess) return nullptr;
-    cached[dev] = static_cast<int*>(ptr);
-  }
-  return cached[dev];
+  if (int* c = cached.get(dev)) return c;
+  void* ptr = nullptr;
+  if (cudaGetSymbolAddress(&ptr, g_splitk_scratch) != cudaSuccess) return nullptr;
+  cached.set(dev, static_cast<int*>(ptr));
+  return static_cast<int*>(ptr);
 }
 }  // namespace
 
@@ -414,13 +413,18 @@ extern "C" int w4a8_gemm_splitk_noalloc(const int8_t* A, int64_t lda, const void
   if (int rc = check_gemm(A, lda, W, ldw, w_kind, M, N, K, epi, C, ldc, &empty)) return rc;
   if (empty) return W4A8_OK;
   if (w_kind != W4A8_W_INT4) return W4A8_ERR_ARG;
-  if (int64_t(M) * int64_t(N) * 4 > int64_t(W4A8_NOALLOC_SCRATCH_BYTES)) return W4A8_ERR_ARG;
-  int* scratch = noalloc_scratch();
-  if (!scratch) return W4A8_ERR_LAUNCH;
   const int sms = device_sms();
   const int tiles_m = (M + kBM - 1) / kBM;
   int bn = N > 128 ? 256 : (N > 64 ? 128 : 64);
   while (bn > 64 && tiles_m * ((N + bn - 1) / bn) < sms) bn >>= 1;
+  // Only a split-K shape touches the scratch array; the others (few-token
+  // GEMV, or enough output tiles to fill the GPU) run unsplit, as w4a8_gemm.
+  int split_bn = 0, kb_per = 0;
+  if (splitk_plan(M, N, K, sms, split_bn, kb_per) == 0)
+    return gemm_w4(A, lda, W, ldw, M, N, K, epi, C, ldc, bn, sms, nullptr, 0, static_cast<cudaStream_t>(stream));
+  if (int64_t(M) * int64_t(N) * 4 > int64_t(W4A8_NOALLOC_SCRATCH_BYTES)) return W4A8_ERR_ARG;
+  int* scratch = noalloc_scratch();
+  if (!scratch) return W4A8_ERR_LAUNCH;
   // gemm_w4 zeroes the M x N sums it uses (cudaMemsetAsync) before the kernel.
   return gemm_w4(A, lda, W, ldw, M, N, K, epi, C, ldc, bn, sms, scratch, W4A8_NOALLOC_SCRATCH_BYTES,
                  static_cast<cudaStream_t>(stream));

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdint>
 #include <cstring>
 
@@ -13,16 +14,32 @@
 
 namespace w4a8 {
 
+// Per-device values looked up once (device ids 0..63) and shared by every
+// host thread. Slots are atomics: threads that race on a first lookup each
+// compute the same value and store it, which is well defined; a zero /
+// null slot means "not looked up yet".
+template <typename T>
+struct PerDevice {
+  std::atomic<T> slot[64];
+  T get(int dev) const { return (dev >= 0 && dev < 64) ? slot[dev].load(std::memory_order_relaxed) : T{}; }
+  void set(int dev, T v) {
+    if (dev >= 0 && dev < 64) slot[dev].store(v, std::memory_order_relaxed);
+  }
+};
+
 inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
+  static std::atomic<PFN_cuTensorMapEncodeTiled_v12000> fn{nullptr};
+  PFN_cuTensorMapEncodeTiled_v12000 f = fn.load(std::memory_order_relaxed);
+  if (!f) {
     void* ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+        q == cudaDriverEntryPointSuccess) {
+      f = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+      fn.store(f, std::memory_order_relaxed);
+    }
   }
-  return fn;
+  return f;
 }
 
 // Encodes a uint8 tiled map. dims/box innermost first; strides (bytes) for
@@ -41,11 +58,11 @@ inline int encode_u8(CUtensorMap* map, const void* ptr, int rank, const uint64_t
 inline int device_sms() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-  static int cached[64] = {0};
-  if (dev >= 0 && dev < 64 && cached[dev]) return cached[dev];
+  static PerDevice<int> cached;
+  if (const int c = cached.get(dev)) return c;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (dev >= 0 && dev < 64) cached[dev] = sms;
+  cached.set(dev, sms);
   return sms;
 }
 

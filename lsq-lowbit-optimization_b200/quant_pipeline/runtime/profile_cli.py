@@ -2,8 +2,13 @@
 scripts/profile_lsq_inference.py with ``--reuse-single-batch``), shaped for
 Nsight Compute: every sub-command builds its inputs once, runs a few
 warm-up launches, then ``--iters`` timed launches with CUDA events, and
-prints one JSON line. Run the same command under ``ncu -k regex:w4a8 -s
-<warmup> -c <n>`` to capture individual launches.
+prints one JSON line. To capture individual launches, run the same command
+(after it has exited 0 on its own) under
+``ncu --clock-control none --metrics gpu__time_duration.sum -k regex:w4a8
+-s <warmup> -c <n>``; without ``--clock-control none`` ncu locks the GPU
+clocks, a setting that outlasts the process. A fuller capture (``--set
+full`` or several sections) should cover one kernel and one to three
+launches of a small case.
 
   python -m quant_pipeline.runtime.profile_cli conv  --n 256 --h 56 --c 64 --o 64 --k 3 --stride 1
   python -m quant_pipeline.runtime.profile_cli gemm  --m 4096 --n 8192 --k 8192

@@ -177,22 +177,41 @@ def conv_unfold_path(x, w_int, a_scale, w_scale, qn, qp, stride, pad, bias=None,
 
 
 # ----------------------------------------------------------- NHWC int8 path
+def _exact_float_type(k: int, amax: int, wmax: int):
+    """Float type whose BLAS product of integer operands is exact: every
+    partial sum is an integer of magnitude <= k * amax * wmax, exact in
+    float32 below 2**24 (in any summation order) and in float64 below 2**53."""
+    return np.float32 if k * amax * wmax < (1 << 24) else np.float64
+
+
 def conv_nhwc_s32(xq: np.ndarray, w_ohwi: np.ndarray, stride: int, pad_h: int, pad_w: int, ho: int,
-                  wo: int) -> np.ndarray:
+                  wo: int, chunk_bytes: int = 1 << 28) -> np.ndarray:
     """Integer conv of NHWC codes with OHWI weights; zero padding top/left
-    pad_h/pad_w, output [n, ho, wo, o] int32."""
+    pad_h/pad_w, output [n, ho, wo, o] int32. Images are lowered a few at a
+    time so that the lowered columns stay below ``chunk_bytes``."""
     n, h, w, c = xq.shape
     o, kh, kw, _ = w_ohwi.shape
     hp = max(h + pad_h, (ho - 1) * stride + kh)
     wp = max(w + pad_w, (wo - 1) * stride + kw)
-    xp = np.zeros((n, hp, wp, c), dtype=np.float64)
-    xp[:, pad_h:pad_h + h, pad_w:pad_w + w, :] = xq
-    cols = np.empty((n, ho, wo, kh, kw, c), dtype=np.float64)
-    for ky in range(kh):
-        for kx in range(kw):
-            cols[:, :, :, ky, kx, :] = xp[:, ky:ky + stride * ho:stride, kx:kx + stride * wo:stride, :]
-    acc = cols.reshape(-1, kh * kw * c) @ w_ohwi.reshape(o, -1).astype(np.float64).T
-    return np.rint(acc).astype(np.int64).astype(np.int32).reshape(n, ho, wo, o)
+    k = kh * kw * c
+    amax = int(np.abs(xq.astype(np.int32)).max()) if xq.size else 0
+    wmax = int(np.abs(w_ohwi.astype(np.int32)).max()) if w_ohwi.size else 0
+    ft = _exact_float_type(k, amax, wmax)
+    wt = np.ascontiguousarray(w_ohwi.reshape(o, -1).astype(ft).T)
+    out = np.empty((n, ho, wo, o), dtype=np.int32)
+    per_img = ho * wo * k * np.dtype(ft).itemsize
+    step = max(1, int(chunk_bytes // max(per_img, 1)))
+    for i0 in range(0, n, step):
+        i1 = min(n, i0 + step)
+        xp = np.zeros((i1 - i0, hp, wp, c), dtype=ft)
+        xp[:, pad_h:pad_h + h, pad_w:pad_w + w, :] = xq[i0:i1]
+        cols = np.empty((i1 - i0, ho, wo, kh, kw, c), dtype=ft)
+        for ky in range(kh):
+            for kx in range(kw):
+                cols[:, :, :, ky, kx, :] = xp[:, ky:ky + stride * ho:stride, kx:kx + stride * wo:stride, :]
+        acc = cols.reshape(-1, k) @ wt
+        out[i0:i1] = np.rint(acc).astype(np.int64).astype(np.int32).reshape(i1 - i0, ho, wo, o)
+    return out
 
 
 def maxpool3x3s2(x: np.ndarray) -> np.ndarray:

@@ -1,8 +1,9 @@
 """Generates the golden fixtures in this directory from the REFERENCE's own
 Python code (peihengzju/lsq-lowbit-optimization), imported from the
-read-only checkout. Run in the build container only:
+read-only checkout, whose path is the one required argument. Run where
+that checkout exists:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path to the reference checkout>
 
 Fixtures (small .npz / .json files) are committed; tests never import the
 reference. What each file pins:
@@ -23,7 +24,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
-sys.path.insert(0, sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+if len(sys.argv) != 2 or not (Path(sys.argv[1]) / "quant_pipeline").is_dir():
+    sys.exit("usage: make_golden.py <path to the reference checkout (the directory holding quant_pipeline/)>")
+sys.path.insert(0, sys.argv[1])
 
 from lsq_standin import build_standin  # noqa: E402
 from quant_pipeline.integration import lsq_adapter  # noqa: E402  (reference package)

@@ -1,0 +1,107 @@
+"""Parity at the headline sizes: the fused low-bit conv at batch 256 and the
+whole ResNet-18 at batch 256.
+
+At these sizes every persistent conv CTA works through dozens of tiles
+(config-2 3x3/s1: 7,168 tiles of 16x8 pixels on 148 CTAs), so the TMEM
+accumulator buffers rotate, their phases flip, the halo ring wraps and
+resident weights are reused across tiles; the smaller cases in
+test_conv_gpu.py give each CTA at most one tile. Integer results are
+compared bit for bit with the oracle (the reference's integer semantics:
+csrc/int4_int8_kernels.cu:19-84 for the product, :109-112 for the
+epilogue, benchmarks/benchmark_inference.py:62-79 for the check pattern).
+"""
+import numpy as np
+import pytest
+import torch
+
+import int4_int8_ext as ext
+from oracle import oracle as orc
+from oracle import resnet_oracle as ro
+from tests.helpers import assert_equal, rand_i4, rand_i8, rng, to_dev
+from tests.test_conv_gpu import run_nhwc_conv
+
+pytestmark = pytest.mark.gpu
+
+# Config 2: [256, 56, 56, 64] int8 NHWC codes of post-ReLU activations, int4
+# weights, per-channel weight scale U[1e-3, 1e-2], bias N(0, 0.01), ReLU,
+# requant to int8 with scale 0.05; plus the stride-2 64->128 downsample and
+# its 1x1 stride-2 shortcut (float32 identity out, as ResNet uses it).
+CFG2 = [
+    # name, n, h, w, c, o, k, stride, pad, fused output
+    ("3x3s1", 256, 56, 56, 64, 64, 3, 1, 1, ext.OUT_S8),
+    ("3x3s2", 256, 56, 56, 64, 128, 3, 2, 1, ext.OUT_S8),
+    ("1x1s2", 256, 56, 56, 64, 128, 1, 2, 0, ext.OUT_F32),
+]
+
+
+@pytest.mark.parametrize("name,n,h,w,c,o,k,stride,pad,fused", CFG2)
+def test_config2_conv_full_size(cuda, name, n, h, w, c, o, k, stride, pad, fused):
+    g = rng(2000 + k * 10 + stride)
+    xq = rand_i8(g, (n, h, w, c), 0, 127)
+    wt = rand_i4(g, (o, k, k, c))
+    s_w = g.uniform(1e-3, 1e-2, o).astype(np.float32)
+    bias = g.normal(0, 0.01, o).astype(np.float32)
+    ho = (h + 2 * pad - k) // stride + 1
+    wo = (w + 2 * pad - k) // stride + 1
+    acc = orc.conv_nhwc_s32(xq, wt, stride, pad, pad, ho, wo)
+    got = run_nhwc_conv(cuda, xq, wt, stride, pad, ho, wo, {}, ext.OUT_S32)
+    assert_equal(got, acc, f"cfg2 {name} int32")
+    del got
+    alpha = (np.float64(0.05) * s_w.astype(np.float64)).astype(np.float32)
+    if fused == ext.OUT_S8:
+        want = orc.quantize(orc.epilogue(acc, alpha, bias, relu=True), 0.05, 0, 127)
+        epi = dict(alpha=to_dev(alpha, cuda), beta=to_dev(bias, cuda), relu=True, out_scale=0.05, qn=0, qp=127)
+    else:
+        want = orc.epilogue(acc, alpha, bias)
+        epi = dict(alpha=to_dev(alpha, cuda), beta=to_dev(bias, cuda))
+    got = run_nhwc_conv(cuda, xq, wt, stride, pad, ho, wo, epi, fused)
+    assert_equal(got, want, f"cfg2 {name} fused epilogue")
+    assert ext.device_error() == 0
+
+
+def test_streamed_int8_conv_many_tiles(cuda):
+    """The layer-3 shape with int8 weights streamed through the ring (no
+    resident weights, 256-wide tiles, two TMEM buffers): 512 tiles."""
+    g = rng(2100)
+    n, h, w, c, o = 256, 14, 14, 256, 256
+    xq = rand_i8(g, (n, h, w, c), 0, 127)
+    wt = rand_i4(g, (o, 3, 3, c))
+    got = run_nhwc_conv(cuda, xq, wt, 1, 1, h, w, {}, ext.OUT_S32, int4=False)
+    assert_equal(got, orc.conv_nhwc_s32(xq, wt, 1, 1, 1, h, w), "layer-3 int8 streamed")
+
+
+def test_two_image_tiles_many(cuda):
+    """The 7x7 stage with two images per tile at batch 256 (128 tiles of
+    512 channels), int4 weights streamed and expanded per k-block."""
+    g = rng(2200)
+    n, h, w, c, o = 256, 7, 7, 512, 512
+    xq = rand_i8(g, (n, h, w, c), 0, 127)
+    wt = rand_i4(g, (o, 3, 3, c))
+    got = run_nhwc_conv(cuda, xq, wt, 1, 1, h, w, {}, ext.OUT_S32)
+    assert_equal(got, orc.conv_nhwc_s32(xq, wt, 1, 1, 1, h, w), "layer-4 pack2 int4")
+
+
+@pytest.fixture(scope="module")
+def resnet18_bs256():
+    from quant_pipeline.runtime.lsq_resnet import build_lsq_resnet, synthetic_images
+
+    model = build_lsq_resnet("resnet18", seed=0)
+    images = synthetic_images(256, seed=0)
+    return model, images, ro.resnet_forward(model, images.numpy())
+
+
+def test_resnet18_bs256_matches_oracle(cuda, resnet18_bs256):
+    """Config 3: the engine at batch 256 (CUDA graph) against the integer
+    oracle; gates rel 1e-3 and top-1 >= 99.9%, and the engine follows the
+    oracle's op order, so the logits are equal bit for bit."""
+    from quant_pipeline.runtime.engine import W4A8ResNetEngine
+
+    model, images, want = resnet18_bs256
+    eng = W4A8ResNetEngine(model, 256, device=cuda, use_graph=True)
+    got = eng.forward(images.to(cuda)).cpu().numpy()
+    eng.release()
+    err, agree = ro.rel_err(got, want), ro.top1_agreement(got, want)
+    print(f"resnet18 bs256: rel_err={err:.3e} top1={agree:.4f} bit_exact={np.array_equal(got, want)}")
+    assert err <= 1e-3 and agree >= 0.999
+    assert np.array_equal(got, want)
+    assert ext.device_error() == 0

@@ -65,3 +65,20 @@ def test_noalloc_rejects_beyond_scratch(cuda):
     out = torch.empty((m, n), dtype=torch.int32, device=cuda)
     epi = ext.make_epilogue(ext.OUT_S32)
     assert _noalloc(x, w, m, n, k, epi, out) == ext.ERR_ARG
+
+
+def test_noalloc_unsplit_shape_beyond_scratch_runs(cuda):
+    """A shape with enough output tiles runs unsplit and never touches the
+    scratch array, so M * N * 4 above its size is accepted; results equal
+    w4a8_gemm."""
+    m, n, k = 256, 8192, 1024
+    assert m * n * 4 > ext.NOALLOC_SCRATCH_BYTES and ext.splitk_workspace_bytes(m, n, k, ext.W_INT4) == 0
+    g = rng(4100)
+    x = rand_i8(g, (m, k))
+    bp = orc.pack_int4(rand_i4(g, (n, k)))
+    xd, wd = to_dev(x, cuda), to_dev(bp, cuda)
+    epi = ext.make_epilogue(ext.OUT_S32)
+    got = torch.zeros((m, n), dtype=torch.int32, device=cuda)
+    assert _noalloc(xd, wd, m, n, k, epi, got) == 0
+    torch.cuda.synchronize()
+    assert_equal(got, orc.int4_int8_gemm(x, bp), "unsplit noalloc")
