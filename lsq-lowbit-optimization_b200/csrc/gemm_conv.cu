@@ -652,11 +652,17 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
                                 : 0u;
   const uint32_t fixed_bytes = pool_bytes + ab_bytes;
   const int budget = kSmemBudget - int(fixed_bytes);
+  // Resident weights also keep the MMA's descriptor table: one 16-byte (A, B)
+  // pair per issued K-step, channel group and halo stage.
+  const int gsteps = (kbpg - 1) * (kBK / 32) + cp.tail_steps;
+  const uint32_t tab_stage = uint32_t(groups * gsteps * 16);
+  uint32_t dtab_bytes = 0;
   p.b_resident = 0;
-  if (p.tiles_n == 1 && bres_bytes + 2 * cp.halo_bytes <= uint32_t(budget)) {
+  if (p.tiles_n == 1 && bres_bytes + 2 * (cp.halo_bytes + tab_stage) + 1024u <= uint32_t(budget)) {
     p.b_resident = 1;
     p.stages = 1;
-    p.halo_stages = std::min<int>(kMaxHaloStages, (budget - bres_bytes) / cp.halo_bytes);
+    p.halo_stages = std::min<int>(kMaxHaloStages, (budget - 1024 - bres_bytes) / (cp.halo_bytes + tab_stage));
+    dtab_bytes = (uint32_t(p.halo_stages) * tab_stage + 1023u) & ~1023u;
     p.bres_tx_bytes = i4 ? bres_bytes / 2 : bres_bytes;
   } else {
     // Deepest halo pipeline (each stage is one tile's input window) that
@@ -672,7 +678,8 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   p.h_off = 0;
   cp.pool_off = p.halo_stages * cp.halo_bytes;
   cp.ab_off = ab_bytes ? cp.pool_off + pool_bytes : 0u;
-  p.b_off = cp.pool_off + pool_bytes + ab_bytes;
+  cp.dtab_off = cp.pool_off + pool_bytes + ab_bytes;
+  p.b_off = cp.dtab_off + dtab_bytes;
   p.bp_off = 0;
   p.tx_bytes = i4 ? p.b_stage_bytes / 2 : p.b_stage_bytes;
   p.tmem_cols = 2 * bn;

@@ -118,6 +118,8 @@ struct ConvParams {
   int n;                   // images
   int pho, pwo;            // pooled output size
   uint32_t pool_off;       // smem offset of the int32 accumulator staging tile
+  uint32_t dtab_off;       // resident weights: smem offset of the MMA descriptor table
+                           // ((A, B) pairs per halo stage, channel group and issued K-step)
   // A-operand descriptor of each 32-byte K-step relative to the halo stage
   // base (start address = offset inside the stage; add stage_addr >> 4).
   uint64_t step_desc[kMaxSteps];
@@ -522,6 +524,72 @@ __device__ __forceinline__ void epilogue16(const EpiParams& e, const EpiConsts& 
   }
 }
 
+// Conv tiles are split into contiguous per-CTA ranges [conv_tile_begin(b),
+// conv_tile_begin(b + 1)): a CTA's consecutive tiles are spatial neighbours,
+// and every role steps its tile coordinates with ConvTile::next instead of
+// dividing (a single-thread control loop pays for each instruction).
+__device__ __forceinline__ int conv_tile_begin(int total, int b, int nb) {
+  return int((long long)total * b / nb);
+}
+
+struct ConvTile {
+  int nt, tw, th, img;  // n-tile, tile column, tile row, image (image pair for two-image tiles)
+  __device__ __forceinline__ void init(const KParams& p, int t) {
+    const int mt = t / p.tiles_n;
+    nt = t - mt * p.tiles_n;
+    const int per_img = p.conv.tiles_h * p.conv.tiles_w;
+    img = mt / per_img;
+    const int rem = mt - img * per_img;
+    th = rem / p.conv.tiles_w;
+    tw = rem - th * p.conv.tiles_w;
+  }
+  __device__ __forceinline__ void next(const KParams& p) {
+    if (++nt == p.tiles_n) {
+      nt = 0;
+      if (++tw == p.conv.tiles_w) {
+        tw = 0;
+        if (++th == p.conv.tiles_h) {
+          th = 0;
+          ++img;
+        }
+      }
+    }
+  }
+  // Moves to tile t, `step` tiles on from the current one (next() for a step of one).
+  __device__ __forceinline__ void advance(const KParams& p, int t, int step) {
+    if (step == 1)
+      next(p);
+    else
+      init(p, t);
+  }
+  // Output addressing of row m (0..127) of this tile; false outside the output.
+  __device__ __forceinline__ bool row(const KParams& p, int m, long long& out_off, long long& prow) const {
+    const ConvParams& c = p.conv;
+    int im, oh, ow;
+    if (c.pack2) {
+      im = 2 * img + ((m >> 3) & 1);
+      oh = m >> 4;
+      ow = m & 7;
+    } else {
+      im = img;
+      oh = th * kTileH + (m >> 3);
+      ow = tw * kTileW + (m & 7);
+    }
+    const long long pix = (long long)oh * c.wo + ow;
+    out_off = (long long)im * p.epi.s_img + pix * p.epi.s_pix;
+    prow = (long long)im * c.ho * c.wo + pix;
+    return im < c.n && oh < c.ho && ow < c.wo;
+  }
+};
+
+// Bounded wait of a whole warp: lane 0 polls, the warp gets the result.
+template <bool kIdle>
+__device__ __forceinline__ bool warp_wait(int lane, uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  int ok = 1;
+  if (lane == 0) ok = mbar_wait_t<kIdle>(bar, parity, abort_flag) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 // Maps (tile m index, row within tile) to output addressing.
 template <bool kConv>
 __device__ __forceinline__ bool row_coords(const KParams& p, int mt, int m, long long& out_off,
@@ -563,8 +631,8 @@ __device__ __forceinline__ bool row_coords(const KParams& p, int mt, int m, long
 // the pooled codes (out) and float32 values (aux).
 template <int BN, int kSetWarps>
 __device__ __forceinline__ void pool_epilogue(const KParams& p, const EpiConsts& k, uint32_t t_addr,
-                                              uint8_t* stage_bytes, int mt, int m, int slice, int slices, int ew,
-                                              int lane, uint64_t* tempty, int bar_id) {
+                                              uint8_t* stage_bytes, const ConvTile& ct, int m, int slice, int slices,
+                                              int ew, int lane, uint64_t* tempty, int bar_id) {
   int32_t* stg = reinterpret_cast<int32_t*>(stage_bytes);
   for (int c0 = slice * (BN / slices); c0 < (slice + 1) * (BN / slices); c0 += 16) {
     uint32_t acc[16];
@@ -580,11 +648,7 @@ __device__ __forceinline__ void pool_epilogue(const KParams& p, const EpiConsts&
   bar_sync(bar_id, kSetWarps * 32);
   const ConvParams& c = p.conv;
   const EpiParams& e = p.epi;
-  const int per_img = c.tiles_h * c.tiles_w;
-  const int img = mt / per_img;
-  const int rem = mt - img * per_img;
-  const int th = rem / c.tiles_w;
-  const int tw = rem - th * c.tiles_w;
+  const int img = ct.img, th = ct.th, tw = ct.tw;
   const int oh0 = th * 2 * kPoolRows - 1, ow0 = tw * 2 * kPoolCols - 1;
   constexpr int kQuads = BN / 4;
   for (int w = ew * 32 + lane; w < kPoolRows * kPoolCols * kQuads; w += kSetWarps * 32) {
@@ -703,7 +767,14 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmW);
-    if constexpr (!kConv) tma_prefetch_desc(&tmA);
+    if constexpr (!kConv) {
+      tma_prefetch_desc(&tmA);
+    } else {
+      tma_prefetch_desc(&tmH0);
+      if (p.conv.n_slots > 1) tma_prefetch_desc(&tmH1);
+      if (p.conv.n_slots > 2) tma_prefetch_desc(&tmH2);
+      if (p.conv.n_slots > 3) tma_prefetch_desc(&tmH3);
+    }
   }
   if (kConv && warp == 2) {
     // Zero the halo buffers once: bytes no box covers stay 0.
@@ -723,6 +794,14 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
   const int total_tiles = p.tiles_m * p.tiles_n;
   const int kbpg = kConv ? p.conv.kb_per_group : p.num_kb;
 
+  // Conv with resident weights: this CTA's contiguous tile range. Otherwise
+  // tiles blockIdx.x + i * gridDim.x: with streamed weights, every CTA then
+  // reads the same weight stages at about the same time, which keeps them in L2.
+  const bool contig = kConv && p.b_resident;
+  const int t_begin = contig ? conv_tile_begin(total_tiles, blockIdx.x, gridDim.x) : int(blockIdx.x);
+  const int t_end = contig ? conv_tile_begin(total_tiles, blockIdx.x + 1, gridDim.x) : total_tiles;
+  const int t_step = contig ? 1 : int(gridDim.x);
+
   if (warp == 0) {
     // ---------------------------- producer ----------------------------------
     if (lane == 0) {
@@ -739,53 +818,61 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
             tma_load_2d(bdst, &tmW, &bar_bres, kb * kBK, 0);
         }
       }
-      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
-        const int mt = t / p.tiles_n;
-        const int nt = t - mt * p.tiles_n;
-        int img = 0, oh0 = 0, ow0 = 0;
-        if constexpr (kConv) {
-          const int per_img = p.conv.tiles_h * p.conv.tiles_w;
-          img = mt / per_img;
-          const int rem = mt - img * per_img;
-          const int th = rem / p.conv.tiles_w;
-          const int tw = rem - th * p.conv.tiles_w;
-          oh0 = p.conv.pool ? th * 2 * kPoolRows - 1 : th * kTileH;
-          ow0 = p.conv.pool ? tw * 2 * kPoolCols - 1 : tw * kTileW;
-        }
-        int g = 0, kb_in_g = 0;
-        for (int kb = 0; ok && kb < p.num_kb; ++kb) {
-          if constexpr (kConv) {
-            if (kb_in_g == 0) {
-              if (!mbar_wait_t<kConv>(&bar_hempty[hs], hph ^ 1, &abort_flag)) { ok = false; break; }
-              mbar_arrive_expect_tx(&bar_hfull[hs], p.conv.halo_tx_bytes);
-              uint8_t* hdst = base + p.h_off + hs * p.conv.halo_bytes;
-              for (int sl = 0; sl < p.conv.n_slots; ++sl) {
-                const CUtensorMap* m = sl == 0 ? &tmH0 : sl == 1 ? &tmH1 : sl == 2 ? &tmH2 : &tmH3;
-                if (p.conv.pack2)  // map dims (c, group, W, N, H): both images' halo rows, interleaved
-                  tma_load_5d(hdst + sl * p.conv.slot_bytes, m, &bar_hfull[hs], 0, g, ow0 + p.conv.slot_qw[sl],
-                              2 * img, oh0 + p.conv.slot_qh[sl]);
-                else
-                  tma_load_5d(hdst + sl * p.conv.slot_bytes, m, &bar_hfull[hs], 0, g, ow0 + p.conv.slot_qw[sl],
-                              oh0 + p.conv.slot_qh[sl], img);
-              }
-              if (++hs == p.halo_stages) { hs = 0; hph ^= 1; }
+      if constexpr (kConv) {
+        // Per tile and channel group: one halo window (a 5-D box per stride
+        // phase), then, with streamed weights, the group's weight stages.
+        const bool resident = p.b_resident != 0, pool = p.conv.pool != 0, pack2 = p.conv.pack2 != 0;
+        const int groups = p.num_kb / kbpg, n_slots = p.conv.n_slots;
+        const int hstages = p.halo_stages, stages = p.stages;
+        const uint32_t htx = p.conv.halo_tx_bytes, hbytes = p.conv.halo_bytes, slot_bytes = p.conv.slot_bytes;
+        ConvTile ct;
+        ct.init(p, t_begin);
+        for (int t = t_begin; ok && t < t_end; t += t_step, ct.advance(p, t, t_step)) {
+          const int oh0 = pool ? ct.th * (2 * kPoolRows) - 1 : ct.th * kTileH;
+          const int ow0 = pool ? ct.tw * (2 * kPoolCols) - 1 : ct.tw * kTileW;
+          int kb = 0;
+          for (int g = 0; ok && g < groups; ++g) {
+            if (!mbar_wait_t<true>(&bar_hempty[hs], hph ^ 1, &abort_flag)) { ok = false; break; }
+            mbar_arrive_expect_tx(&bar_hfull[hs], htx);
+            uint8_t* hdst = base + p.h_off + hs * hbytes;
+            for (int sl = 0; sl < n_slots; ++sl) {
+              const CUtensorMap* m = sl == 0 ? &tmH0 : sl == 1 ? &tmH1 : sl == 2 ? &tmH2 : &tmH3;
+              if (pack2)  // map dims (c, group, W, N, H): both images' halo rows, interleaved
+                tma_load_5d(hdst + sl * slot_bytes, m, &bar_hfull[hs], 0, g, ow0 + p.conv.slot_qw[sl], 2 * ct.img,
+                            oh0 + p.conv.slot_qh[sl]);
+              else
+                tma_load_5d(hdst + sl * slot_bytes, m, &bar_hfull[hs], 0, g, ow0 + p.conv.slot_qw[sl],
+                            oh0 + p.conv.slot_qh[sl], ct.img);
+            }
+            if (++hs == hstages) { hs = 0; hph ^= 1; }
+            if (resident) continue;
+            for (int i = 0; i < kbpg; ++i, ++kb) {
+              if (!mbar_wait_t<true>(&bar_empty[s], ph ^ 1, &abort_flag)) { ok = false; break; }
+              mbar_arrive_expect_tx(&bar_full[s], p.tx_bytes);
+              uint8_t* bdst = base + p.b_off + s * p.b_stage_bytes;
+              if constexpr (kInt4)
+                tma_load_2d(bdst + BN * (kBK / 2), &tmW, &bar_full[s], kb * (kBK / 2), ct.nt * BN);
+              else
+                tma_load_2d(bdst, &tmW, &bar_full[s], kb * kBK, ct.nt * BN);
+              if (++s == stages) { s = 0; ph ^= 1; }
             }
           }
-          if (kConv && p.b_resident) {
-            if (++kb_in_g == kbpg) { kb_in_g = 0; ++g; }
-            continue;
-          }
-          if (!mbar_wait_t<kConv>(&bar_empty[s], ph ^ 1, &abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&bar_full[s], p.tx_bytes);
-          if constexpr (!kConv)
+        }
+      } else {
+        for (int t = t_begin; ok && t < t_end; t += t_step) {
+          const int mt = t / p.tiles_n;
+          const int nt = t - mt * p.tiles_n;
+          for (int kb = 0; ok && kb < p.num_kb; ++kb) {
+            if (!mbar_wait(&bar_empty[s], ph ^ 1, &abort_flag)) { ok = false; break; }
+            mbar_arrive_expect_tx(&bar_full[s], p.tx_bytes);
             tma_load_2d(base + p.a_off + s * p.a_stage_bytes, &tmA, &bar_full[s], kb * kBK, mt * kBM);
-          uint8_t* bdst = base + p.b_off + s * p.b_stage_bytes;
-          if constexpr (kInt4)
-            tma_load_2d(bdst + BN * (kBK / 2), &tmW, &bar_full[s], kb * (kBK / 2), nt * BN);
-          else
-            tma_load_2d(bdst, &tmW, &bar_full[s], kb * kBK, nt * BN);
-          if (++s == p.stages) { s = 0; ph ^= 1; }
-          if (kConv && ++kb_in_g == kbpg) { kb_in_g = 0; ++g; }
+            uint8_t* bdst = base + p.b_off + s * p.b_stage_bytes;
+            if constexpr (kInt4)
+              tma_load_2d(bdst + BN * (kBK / 2), &tmW, &bar_full[s], kb * (kBK / 2), nt * BN);
+            else
+              tma_load_2d(bdst, &tmW, &bar_full[s], kb * kBK, nt * BN);
+            if (++s == p.stages) { s = 0; ph ^= 1; }
+          }
         }
       }
       // Drain: every TMA this thread issued has landed before the CTA exits.
@@ -812,106 +899,149 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------ MMA ------------------------------------
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_i8(kBM, BN);
-      // Descriptor templates (start address 0): the issue loop only adds the
-      // stage / halo base, keeping this single thread's per-MMA work short
-      // enough to keep the tensor core fed.
-      const uint64_t sw128_tmpl = make_smem_desc(0, 16, 1024, kLayoutSw128);
-      const uint32_t a_stage0 = (base_u32 + p.a_off) >> 4, b_stage0 = (base_u32 + p.b_off) >> 4;
-      const uint32_t a_step = p.a_stage_bytes >> 4, b_step = p.b_stage_bytes >> 4;
-      int s = 0, hs = 0, it = 0;
-      uint32_t ph = 0, hph = 0;
+    constexpr uint32_t idesc = make_idesc_i8(kBM, BN);
+    // Descriptor templates (start address 0): the issue loop only adds the
+    // stage / halo base.
+    const uint64_t sw128_tmpl = make_smem_desc(0, 16, 1024, kLayoutSw128);
+    const uint32_t a_stage0 = (base_u32 + p.a_off) >> 4, b_stage0 = (base_u32 + p.b_off) >> 4;
+    const uint32_t a_step = p.a_stage_bytes >> 4, b_step = p.b_stage_bytes >> 4;
+    if constexpr (kConv) {
+      // The whole warp runs the issue loop and one elected lane issues each
+      // MMA and commit: a converged warp issues its instructions markedly
+      // faster than one lane looping alone while the rest of the warp waits.
+      const bool resident = p.b_resident != 0;
+      const int groups = p.num_kb / kbpg, hstages = p.halo_stages;
+      // Resident weights: the (A, B) descriptor pair of every (halo stage,
+      // channel group, K-step) is built once into shared memory, so an MMA
+      // costs one 16-byte shared load and its issue. The zero-weight padding
+      // steps of a group's last k-block are not issued.
+      const int gsteps = (kbpg - 1) * 4 + p.conv.tail_steps;
+      ulonglong2* dtab = reinterpret_cast<ulonglong2*>(base + p.conv.dtab_off);
+      if (resident) {
+        const int per_stage = groups * gsteps;
+        for (int i = lane; i < hstages * per_stage; i += 32) {
+          const int h = i / per_stage, r = i - h * per_stage, g = r / gsteps, j = r - g * gsteps;
+          const uint32_t halo_lo = (base_u32 + p.h_off + uint32_t(h) * p.conv.halo_bytes) >> 4;
+          const uint32_t kb = uint32_t(g * kbpg + (j >> 2));
+          dtab[i] = make_ulonglong2(p.conv.step_desc[j] + halo_lo,
+                                    sw128_tmpl + (b_stage0 + kb * b_step) + 2 * uint32_t(j & 3));
+        }
+        __syncwarp();
+      }
+      int hs = 0, buf = 0;
+      uint32_t hph = 0, tph = 0;
       bool ok = true;
-      const bool resident = kConv && p.b_resident;
-      if (resident) ok = mbar_wait_t<kConv>(kInt4 ? &bar_bready : &bar_bres, 0, &abort_flag);
-      // The inner loops carry no break: a failed wait clears `ok` and sets the
-      // CTA's abort flag (so every later wait gives up within a few hundred
-      // polls), the tile's remaining MMAs read in-bounds shared memory, and
-      // the tile loop stops. Inner loops without exits issue markedly faster.
-      for (int t = blockIdx.x; ok && t < total_tiles; t += gridDim.x, ++it) {
-        const int buf = it % kNB;
-        if (!mbar_wait_t<kConv>(&bar_tempty[buf], ((it / kNB) & 1) ^ 1, &abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BN;
-        if constexpr (kConv) {
-          const int groups = p.num_kb / kbpg;
+      if (resident) {
+        ok = warp_wait<true>(lane, kInt4 ? &bar_bready : &bar_bres, 0, &abort_flag);
+        // The inner loops carry no break: a failed wait clears `ok` and sets
+        // the CTA's abort flag (so every later wait gives up within a few
+        // hundred polls), the tile's remaining MMAs read in-bounds shared
+        // memory, and the tile loop stops.
+        for (int t = t_begin; ok && t < t_end; t += t_step) {
+          if (!warp_wait<true>(lane, &bar_tempty[buf], tph ^ 1, &abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + buf * BN;
+          for (int g = 0; g < groups; ++g) {
+            ok &= warp_wait<true>(lane, &bar_hfull[hs], hph, &abort_flag);
+            tc_fence_after();
+            // The next pair is loaded before the current MMA issues: the MMA
+            // asm's memory clobber would otherwise order the load after it
+            // and expose its latency once per MMA. (Loading four pairs and
+            // then issuing their MMAs back to back measured slower.)
+            const ulonglong2* e = dtab + (hs * groups + g) * gsteps;
+            ulonglong2 d = e[0];
+            ulonglong2 dn = e[gsteps > 1 ? 1 : 0];
+            mma_i8_ss_elect(d_tmem, d.x, d.y, idesc, g != 0 ? 1u : 0u);
+            for (int j = 1; j < gsteps; ++j) {
+              d = dn;
+              dn = e[j + 1 < gsteps ? j + 1 : j];
+              mma_i8_ss_elect(d_tmem, d.x, d.y, idesc, 1u);
+            }
+            mma_commit_elect(&bar_hempty[hs]);
+            if (++hs == hstages) { hs = 0; hph ^= 1; }
+          }
+          mma_commit_elect(&bar_tfull[buf]);
+          if (++buf == kNB) { buf = 0; tph ^= 1; }
+        }
+        // Drain: all tcgen05 ops of this warp complete before TMEM is freed.
+        mma_commit_elect(&bar_drain);
+      } else if (lane == 0) {
+        // Streamed weights: one lane waits for every weight stage and issues
+        // that k-block's four MMAs.
+        int s = 0;
+        uint32_t ph = 0;
+        for (int t = t_begin; ok && t < t_end; t += t_step) {
+          if (!mbar_wait_t<true>(&bar_tempty[buf], tph ^ 1, &abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + buf * BN;
           int kb = 0;
           for (int g = 0; g < groups; ++g) {
-            ok &= mbar_wait_t<kConv>(&bar_hfull[hs], hph, &abort_flag);
+            ok &= mbar_wait_t<true>(&bar_hfull[hs], hph, &abort_flag);
             tc_fence_after();
             const uint32_t halo_lo = (base_u32 + p.h_off + hs * p.conv.halo_bytes) >> 4;
             // A k-block's four step descriptors are loaded before its MMAs
-            // issue, and the next block's while they issue: the MMA asm's
-            // memory clobber would otherwise order each load after the
-            // previous MMA and expose its latency once per MMA.
+            // issue, and the next block's while they issue.
             const uint64_t* sd = p.conv.step_desc;
             uint64_t dn0 = sd[0], dn1 = sd[1], dn2 = sd[2], dn3 = sd[3];
-            if (resident) {
-              // Resident weights: the zero-weight padding steps of the
-              // group's last k-block are not issued.
-              for (int i = 0; i < kbpg - 1; ++i, ++kb) {
-                const uint64_t d0 = dn0 + halo_lo, d1 = dn1 + halo_lo, d2 = dn2 + halo_lo, d3 = dn3 + halo_lo;
-                const uint64_t* nx = sd + 4 * (i + 1);
-                dn0 = nx[0];
-                dn1 = nx[1];
-                dn2 = nx[2];
-                dn3 = nx[3];
-                const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(kb) * b_step);
-                mma_i8_ss(d_tmem, d0, b_desc0, idesc, kb != 0 ? 1u : 0u);
-                mma_i8_ss(d_tmem, d1, b_desc0 + 2, idesc, 1u);
-                mma_i8_ss(d_tmem, d2, b_desc0 + 4, idesc, 1u);
-                mma_i8_ss(d_tmem, d3, b_desc0 + 6, idesc, 1u);
-              }
-              const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(kb) * b_step);
-              const int tail = p.conv.tail_steps;
-              mma_i8_ss(d_tmem, dn0 + halo_lo, b_desc0, idesc, kb != 0 ? 1u : 0u);
-              if (tail > 1) mma_i8_ss(d_tmem, dn1 + halo_lo, b_desc0 + 2, idesc, 1u);
-              if (tail > 2) mma_i8_ss(d_tmem, dn2 + halo_lo, b_desc0 + 4, idesc, 1u);
-              if (tail > 3) mma_i8_ss(d_tmem, dn3 + halo_lo, b_desc0 + 6, idesc, 1u);
-              ++kb;
-            } else {
-              for (int i = 0; i < kbpg; ++i, ++kb) {
-                const uint64_t d0 = dn0 + halo_lo, d1 = dn1 + halo_lo, d2 = dn2 + halo_lo, d3 = dn3 + halo_lo;
-                const uint64_t* nx = sd + 4 * min(i + 1, kbpg - 1);
-                dn0 = nx[0];
-                dn1 = nx[1];
-                dn2 = nx[2];
-                dn3 = nx[3];
-                ok &= mbar_wait_t<kConv>(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag);
-                tc_fence_after();
-                const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(s) * b_step);
-                mma_i8_ss(d_tmem, d0, b_desc0, idesc, kb != 0 ? 1u : 0u);
-                mma_i8_ss(d_tmem, d1, b_desc0 + 2, idesc, 1u);
-                mma_i8_ss(d_tmem, d2, b_desc0 + 4, idesc, 1u);
-                mma_i8_ss(d_tmem, d3, b_desc0 + 6, idesc, 1u);
-                mma_commit(&bar_empty[s]);
-                if (++s == p.stages) { s = 0; ph ^= 1; }
-              }
+            for (int i = 0; i < kbpg; ++i, ++kb) {
+              const uint64_t d0 = dn0 + halo_lo, d1 = dn1 + halo_lo, d2 = dn2 + halo_lo, d3 = dn3 + halo_lo;
+              const uint64_t* nx = sd + 4 * min(i + 1, kbpg - 1);
+              dn0 = nx[0];
+              dn1 = nx[1];
+              dn2 = nx[2];
+              dn3 = nx[3];
+              ok &= mbar_wait_t<true>(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag);
+              tc_fence_after();
+              const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(s) * b_step);
+              mma_i8_ss(d_tmem, d0, b_desc0, idesc, kb != 0 ? 1u : 0u);
+              mma_i8_ss(d_tmem, d1, b_desc0 + 2, idesc, 1u);
+              mma_i8_ss(d_tmem, d2, b_desc0 + 4, idesc, 1u);
+              mma_i8_ss(d_tmem, d3, b_desc0 + 6, idesc, 1u);
+              mma_commit(&bar_empty[s]);
+              if (++s == p.stages) { s = 0; ph ^= 1; }
             }
             mma_commit(&bar_hempty[hs]);
-            if (++hs == p.halo_stages) { hs = 0; hph ^= 1; }
+            if (++hs == hstages) { hs = 0; hph ^= 1; }
           }
-        } else {
-          for (int kb = 0; kb < p.num_kb; ++kb) {
-            ok &= mbar_wait_t<kConv>(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag);
-            tc_fence_after();
-            const uint64_t a_desc0 = sw128_tmpl + (a_stage0 + uint32_t(s) * a_step);
-            const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(s) * b_step);
+          mma_commit(&bar_tfull[buf]);
+          if (++buf == kNB) { buf = 0; tph ^= 1; }
+        }
+        mma_commit(&bar_drain);
+      }
+      if (lane == 0) {
+        const unsigned long long w0 = global_timer_ns();
+        while (!mbar_try_wait(&bar_drain, 0))
+          if (global_timer_ns() - w0 > kWaitLimitNs) { atomicOr(p.err, kErrTimeoutDrain); break; }
+        if (!ok) atomicOr(p.err, kErrTimeoutMma);
+      }
+      __syncwarp();
+    } else if (lane == 0) {
+      int s = 0, it = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = t_begin; ok && t < t_end; t += t_step, ++it) {
+        const int buf = it % kNB;
+        if (!mbar_wait(&bar_tempty[buf], ((it / kNB) & 1) ^ 1, &abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          ok &= mbar_wait(kInt4 ? &bar_ready[s] : &bar_full[s], ph, &abort_flag);
+          tc_fence_after();
+          const uint64_t a_desc0 = sw128_tmpl + (a_stage0 + uint32_t(s) * a_step);
+          const uint64_t b_desc0 = sw128_tmpl + (b_stage0 + uint32_t(s) * b_step);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              mma_i8_ss(d_tmem, a_desc0 + 2 * j, b_desc0 + 2 * j, idesc, (kb | j) != 0 ? 1u : 0u);
-            mma_commit(&bar_empty[s]);
-            if (++s == p.stages) { s = 0; ph ^= 1; }
-          }
+          for (int j = 0; j < 4; ++j)
+            mma_i8_ss(d_tmem, a_desc0 + 2 * j, b_desc0 + 2 * j, idesc, (kb | j) != 0 ? 1u : 0u);
+          mma_commit(&bar_empty[s]);
+          if (++s == p.stages) { s = 0; ph ^= 1; }
         }
         mma_commit(&bar_tfull[buf]);
       }
       // Drain: all tcgen05 ops of this thread complete before TMEM is freed.
       mma_commit(&bar_drain);
-      const unsigned long long t0 = global_timer_ns();
+      const unsigned long long w0 = global_timer_ns();
       while (!mbar_try_wait(&bar_drain, 0))
-        if (global_timer_ns() - t0 > kWaitLimitNs) { atomicOr(p.err, kErrTimeoutDrain); break; }
+        if (global_timer_ns() - w0 > kWaitLimitNs) { atomicOr(p.err, kErrTimeoutDrain); break; }
       if (!ok) atomicOr(p.err, kErrTimeoutMma);
     }
   } else if (warp >= 4 && warp < 4 + kEpiWarps) {
@@ -940,41 +1070,54 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       sa = p.epi.alpha ? a_s : nullptr;
       sb = p.epi.beta ? b_s : nullptr;
     }
-    int it = set;
-    for (int t = blockIdx.x + set * gridDim.x; t < total_tiles; t += kNB * gridDim.x, it += kNB) {
-      const int buf = set;
-      if (p.epi.residual && !(kConv && p.conv.pool)) {
+    // This warp set takes every kNB-th tile of the CTA's sequence (buffer `set`).
+    const int buf = set;
+    uint32_t tph = 0;
+    ConvTile ct;
+    if (kConv && t_begin + set * t_step < t_end) ct.init(p, t_begin + set * t_step);
+    for (int t = t_begin + set * t_step; t < t_end; t += kNB * t_step, tph ^= 1) {
+      int mt = 0, nt = 0;
+      if constexpr (!kConv) {
+        mt = t / p.tiles_n;
+        nt = t - mt * p.tiles_n;
+      } else {
+        nt = ct.nt;
+      }
+      long long out_off = 0, prow = 0;
+      bool valid;
+      if constexpr (kConv)
+        valid = ct.row(p, m, out_off, prow);
+      else
+        valid = row_coords<false>(p, mt, m, out_off, prow);
+      if (p.epi.residual && !(kConv && p.conv.pool) && valid) {
         // The float32 identity rows of this thread's pixel are pulled into L2
         // while the MMA still works on the tile, so the epilogue's loads hit.
-        const int mt0 = t / p.tiles_n, nt0 = t - mt0 * p.tiles_n;
-        long long o0 = 0, pr0 = 0;
-        if (row_coords<kConv>(p, mt0, m, o0, pr0)) {
-          const char* r = reinterpret_cast<const char*>(p.epi.residual + pr0 * p.epi.res_ld + nt0 * BN);
-          const int nbytes = 4 * min(BN, p.epi.n_total - nt0 * BN);
-          for (int off = slice * 128; off < nbytes; off += 128 * kSlices)
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(r + off));
-        }
+        const char* r = reinterpret_cast<const char*>(p.epi.residual + prow * p.epi.res_ld + nt * BN);
+        const int nbytes = 4 * min(BN, p.epi.n_total - nt * BN);
+        for (int off = slice * 128; off < nbytes; off += 128 * kSlices)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(r + off));
       }
       int ok = 1;
-      if (lane == 0) ok = mbar_wait_idle(&bar_tfull[buf], (it / kNB) & 1, &abort_flag) ? 1 : 0;
+      if (lane == 0) ok = mbar_wait_idle(&bar_tfull[buf], tph, &abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
         if (lane == 0) atomicOr(p.err, kErrTimeoutEpilogue);
         break;
       }
       tc_fence_after();
-      const int mt = t / p.tiles_n;
-      const int nt = t - mt * p.tiles_n;
       if constexpr (kConv && BN == 64 && !kInt4) {  // the fused pool: 8-bit weights, <= 64 channels
         if (p.conv.pool) {
           pool_epilogue<BN, kSetWarps>(p, k, tmem_base + (uint32_t(q * 32) << 16) + buf * BN,
-                                       base + p.conv.pool_off + set * kPoolStageBytes, mt, m, slice, kSlices,
+                                       base + p.conv.pool_off + set * kPoolStageBytes, ct, m, slice, kSlices,
                                        (warp - 4) % kSetWarps, lane, &bar_tempty[buf], 2 + set);
+          if (contig) {
+            for (int i = 0; i < kNB; ++i) ct.next(p);
+          } else if (t + kNB * t_step < t_end) {
+            ct.init(p, t + kNB * t_step);
+          }
           continue;
         }
       }
-      long long out_off = 0, prow = 0;
-      const bool valid = row_coords<kConv>(p, mt, m, out_off, prow);
       const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + buf * BN;
 #pragma unroll 1
       for (int c0 = slice * (BN / kSlices); c0 < (slice + 1) * (BN / kSlices); c0 += 16) {
@@ -988,6 +1131,13 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&bar_tempty[buf]);
+      if constexpr (kConv) {
+        if (contig) {
+          for (int i = 0; i < kNB; ++i) ct.next(p);
+        } else if (t + kNB * t_step < t_end) {
+          ct.init(p, t + kNB * t_step);
+        }
+      }
     }
   } else if (warp >= kUnpackWarp0 && kInt4) {
     // ------------------------------ unpack ---------------------------------
@@ -1020,9 +1170,11 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       return got != 0;
     };
     if (resident) ok = bar_and(bar_id, kGT, wait_warp(&bar_bres, 0));
-    const int passes = resident ? 1 : total_tiles;  // resident weights: one pass over the k-blocks
-    uint32_t q = 0;                                  // k-block sequence number of this CTA
-    for (int t = resident ? 0 : int(blockIdx.x); ok && t < passes; t += resident ? 1 : int(gridDim.x)) {
+    // Resident weights: one pass over the k-blocks; otherwise one per tile of
+    // this CTA's sequence.
+    const int t0 = resident ? 0 : t_begin, t1 = resident ? 1 : t_end, ts = resident ? 1 : t_step;
+    uint32_t q = 0;  // k-block sequence number of this CTA
+    for (int t = t0; ok && t < t1; t += ts) {
       for (int kb = 0; kb < p.num_kb; ++kb, ++q) {
         if (int(q % kUnpackGroups) != ug) continue;
         const uint32_t s = resident ? uint32_t(kb) : q % uint32_t(p.stages);
