@@ -64,6 +64,9 @@ CONV_CASES = [
     (2, 9, 13, 32, 48, 1, 1, 0),
     (2, 11, 9, 32, 80, 3, 1, 1),
     (2, 9, 9, 384, 64, 3, 2, 1),
+    # odd tile counts (3 and 15 tiles): the second CTA of the last CTA pair has no tile
+    (1, 16, 24, 64, 64, 3, 1, 1),
+    (3, 40, 20, 64, 128, 3, 1, 1),
 ]
 
 

@@ -105,3 +105,51 @@ def test_resnet18_bs256_matches_oracle(cuda, resnet18_bs256):
     assert err <= 1e-3 and agree >= 0.999
     assert np.array_equal(got, want)
     assert ext.device_error() == 0
+
+
+def test_resnet18_bs256_vs_converted_model_forward(cuda, resnet18_bs256):
+    """The engine against the reference's own model structure at batch 256:
+    convert_lsq_modules, then the converted model's forward (Int4 conv
+    modules on float32 NCHW with torch BatchNorm, ReLU, residual add,
+    max / average pooling, and the 8-bit stem and classifier left as LSQ
+    fake-quant float layers, as the reference leaves them;
+    quant_pipeline/integration/lsq_adapter.py:192-234,
+    quant_pipeline/ops/int4_conv2d.py:137-201), TF32 off.
+
+    That forward rounds differently from exact integer arithmetic in three
+    places: the float stem convolution, BatchNorm applied after the
+    conv's float epilogue instead of folded into it, and torch's reduction
+    order in the average pool. A rounding difference that lands on a
+    quantisation boundary moves one activation code by one step, and one
+    code step at the classifier input moves a logit by about 1e-2 of the
+    largest logit, so the max-abs relative error is about 8e-3 whatever the
+    kernels do (measured per source on a B200). The gates are therefore
+    top-1 agreement >= 99.9% (north_star's), the mean absolute error over
+    the largest logit <= 1e-3, and the max-abs relative error <= 2e-2."""
+    import copy
+
+    from quant_pipeline.integration import convert_lsq_modules
+    from quant_pipeline.runtime.engine import W4A8ResNetEngine
+
+    model, images, _ = resnet18_bs256
+    eng = W4A8ResNetEngine(model, 256, device=cuda, use_graph=True)
+    got = eng.forward(images.to(cuda)).cpu().numpy()
+    eng.release()
+    conv = copy.deepcopy(model)
+    results = convert_lsq_modules(conv, convert_conv=True)
+    assert sum(r.converted for r in results) == 19
+    conv = conv.to(cuda)
+    tf32 = (torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32)
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        with torch.no_grad():
+            want = conv(images.to(cuda)).cpu().numpy()
+    finally:
+        torch.backends.cudnn.allow_tf32, torch.backends.cuda.matmul.allow_tf32 = tf32
+    err, agree = ro.rel_err(got, want), ro.top1_agreement(got, want)
+    mean_err = float(np.mean(np.abs(got - want)) / np.max(np.abs(want)))
+    print(f"resnet18 bs256 vs converted forward: rel_err={err:.3e} mean_err={mean_err:.3e} top1={agree:.4f}")
+    assert agree >= 0.999
+    assert mean_err <= 1e-3
+    assert err <= 2e-2
