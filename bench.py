@@ -631,8 +631,24 @@ def main():
         return
     if world > 1:
         torch.cuda.set_device(local_rank)
-        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=120),
-                                             device_id=torch.device("cuda", local_rank))
+        # NCCL prints its version line to stdout when the communicator is
+        # created (eagerly here, device_id given); it goes to stderr so that
+        # rank 0's stdout carries the one JSON line.
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                                 device_id=torch.device("cuda", local_rank))
+            torch.distributed.barrier()
+            torch.cuda.synchronize()
+        finally:
+            import ctypes
+
+            ctypes.CDLL(None).fflush(None)  # C stdio buffers (NCCL's printf) go out before fd 1 is restored
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     try:
         run_ours(args, rank, world, local_rank)
     finally:
