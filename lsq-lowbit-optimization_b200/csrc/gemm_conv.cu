@@ -27,10 +27,10 @@ namespace {
 constexpr int kSmemAttr = 226 * 1024;         // dynamic smem requested per CTA
 constexpr int kSmemBudget = kSmemAttr - 1024;  // minus base-alignment slack
 
-template <int BN, bool I4, bool CV>
+template <int BN, bool I4, bool CV, bool PL = false>
 int launch_t(const CUtensorMap& tA, const CUtensorMap& tW, const CUtensorMap* tH, const KParams& p, int grid,
              cudaStream_t st) {
-  auto kern = w4a8_mma_kernel<BN, I4, CV>;
+  auto kern = w4a8_mma_kernel<BN, I4, CV, PL>;
   static PerDevice<bool> attr_done;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -514,6 +514,11 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   if (g->pool && (i4 || g->o > 64 || g->out_layout != W4A8_LAYOUT_NHWC || epi->residual ||
                   (epi->out_kind != W4A8_OUT_S8 && epi->out_kind != W4A8_OUT_F32) || (g->o % 4)))
     return W4A8_ERR_UNSUPPORTED;
+  // The pooled epilogue reads alpha / beta and stores in 4-channel vectors.
+  if (g->pool && ((reinterpret_cast<uintptr_t>(out) & (epi->out_kind == W4A8_OUT_F32 ? 15 : 3)) || (g->ldo % 4) ||
+                  (epi->aux && ((reinterpret_cast<uintptr_t>(epi->aux) & 15) || (epi->aux_ld % 4))) ||
+                  (reinterpret_cast<uintptr_t>(epi->alpha) & 15) || (reinterpret_cast<uintptr_t>(epi->beta) & 15)))
+    return W4A8_ERR_ALIGN;
   if (g->n == 0) return W4A8_OK;
   if (!x || !W || !out) return W4A8_ERR_ARG;
   const int s = g->stride;
@@ -580,6 +585,8 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   cp.a_layout = cg == 128 ? kLayoutSw128 : cg == 64 ? kLayoutSw64 : cg == 32 ? kLayoutSw32 : kLayoutNone;
   cp.halo_w = kTileW + span_w;
   cp.halo_h = sub_h + span_h;
+  // One TMA request per halo row instead of one per 16-byte pixel.
+  cp.wc_bytes = (g->c == 16 && s == 1 && !cp.pack2 && cp.halo_w * 16 <= 256) ? 16 : 0;
   if (cp.halo_w > 256 || cp.halo_h > 256) return W4A8_ERR_UNSUPPORTED;
   cp.slot_bytes = (uint32_t(img_mult * cp.halo_w * cp.halo_h * cg) + 1023u) & ~1023u;
   int slot_of[2][2] = {{-1, -1}, {-1, -1}};
@@ -641,16 +648,15 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   // at least two halo stages, the CTA loads and unpacks the weights once and
   // then streams only input halos.
   const uint32_t bres_bytes = uint32_t(p.num_kb) * per_stage;
-  // The fused pool stages one tile of int32 accumulators (128 x 68 words)
-  // per epilogue warp set.
-  const uint32_t pool_bytes = g->pool ? uint32_t(acc_buffers(bn, true)) * kPoolStageBytes : 0u;
   // The epilogue's shared-memory copies of alpha and beta (not with the pool,
-  // whose epilogue reads them per pooled pixel).
+  // whose threads each hold their channel's pair in registers).
   cp.ab_pitch = (g->o + 15) & ~15;
   const uint32_t ab_bytes = (!g->pool && (epi->alpha || epi->beta) && g->o <= 1024)
                                 ? (uint32_t(8 * cp.ab_pitch) + 1023u) & ~1023u
                                 : 0u;
-  const uint32_t fixed_bytes = pool_bytes + ab_bytes;
+  // The pooled conv stages each epilogue set's pooled outputs for vector stores.
+  const uint32_t pool_bytes = g->pool ? 4u * kPoolStageBytes : 0u;
+  const uint32_t fixed_bytes = ab_bytes + pool_bytes;
   const int budget = kSmemBudget - int(fixed_bytes);
   // Resident weights also keep the MMA's descriptor table: one 16-byte (A, B)
   // pair per issued K-step, channel group and halo stage.
@@ -665,10 +671,11 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
     dtab_bytes = (uint32_t(p.halo_stages) * tab_stage + 1023u) & ~1023u;
     p.bres_tx_bytes = i4 ? bres_bytes / 2 : bres_bytes;
   } else {
+    if (g->pool) return W4A8_ERR_UNSUPPORTED;  // the pooled conv keeps its weights resident
     // Deepest halo pipeline (each stage is one tile's input window) that
     // still leaves at least three weight stages.
     p.stages = 0;
-    for (int hs = kMaxHaloStages; hs >= 1 && p.stages < 3; --hs) {
+    for (int hs = 6; hs >= 1 && p.stages < 3; --hs) {
       p.halo_stages = hs;
       p.stages = pick_stages(per_stage, hs * cp.halo_bytes + fixed_bytes);
     }
@@ -676,9 +683,10 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   }
   p.a_off = 0;
   p.h_off = 0;
-  cp.pool_off = p.halo_stages * cp.halo_bytes;
-  cp.ab_off = ab_bytes ? cp.pool_off + pool_bytes : 0u;
-  cp.dtab_off = cp.pool_off + pool_bytes + ab_bytes;
+  const uint32_t halo_end = uint32_t(p.halo_stages) * cp.halo_bytes;
+  cp.ab_off = ab_bytes ? halo_end : 0u;
+  cp.pool_off = halo_end + ab_bytes;
+  cp.dtab_off = halo_end + ab_bytes + pool_bytes;
   p.b_off = cp.dtab_off + dtab_bytes;
   p.bp_off = 0;
   p.tx_bytes = i4 ? p.b_stage_bytes / 2 : p.b_stage_bytes;
@@ -725,8 +733,18 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
     const uint64_t str[4] = {uint64_t(cg), ws, cp.pack2 ? ns_ : hs, cp.pack2 ? hs : ns_};
     const uint32_t box[5] = {uint32_t(cg), 1, uint32_t(cp.halo_w), cp.pack2 ? 2u : uint32_t(cp.halo_h),
                              cp.pack2 ? uint32_t(cp.halo_h) : 1u};
+    if (cp.wc_bytes) {
+      // 16-byte pixels at stride 1: (W * C, 1, 1, H, N), one box row per halo row.
+      const uint64_t wc = uint64_t(g->w) * g->c;
+      const uint64_t mdims[5] = {wc, 1, 1, uint64_t(g->h), uint64_t(g->n)};
+      const uint64_t mstr[4] = {wc, wc, wc, uint64_t(g->h) * wc};
+      const uint32_t mbox[5] = {uint32_t(cp.halo_w * g->c), 1, 1, uint32_t(cp.halo_h), 1};
+      if (encode_u8(&tH[sl], base, 5, mdims, mstr, mbox, swz)) return W4A8_ERR_TENSORMAP;
+      continue;
+    }
     if (encode_u8(&tH[sl], base, 5, dims, str, box, swz)) return W4A8_ERR_TENSORMAP;
   }
   const int grid = std::min(p.tiles_m * p.tiles_n, sms);
+  if (g->pool) return launch_t<64, false, true, true>(tA, tW, tH, p, grid, static_cast<cudaStream_t>(stream));
   return launch(i4, true, bn, tA, tW, tH, p, grid, static_cast<cudaStream_t>(stream));
 }

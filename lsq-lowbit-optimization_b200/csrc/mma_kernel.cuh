@@ -57,14 +57,17 @@ __host__ __device__ constexpr uint32_t tmem_columns(int bn, bool conv) {
   return cols;
 }
 constexpr int kMaxStages = 8;
-constexpr int kMaxHaloStages = 6;
+constexpr int kMaxHaloStages = 12;
 constexpr int kMaxSteps = 64;     // conv MMA K-steps (32 B) per channel group
 constexpr int kTileH = 16;        // conv: output rows per tile (one 8-row core group each)
 constexpr int kTileW = 8;         // conv: output columns per tile
 // Fused max pool: a 16x8 conv tile at origin (14*th - 1, 6*tw - 1) holds
 // every 3x3/s2 window of a 7x3 block of pooled outputs.
-constexpr int kPoolRows = 7, kPoolCols = 3, kPoolPitch = 68;  // staging row pitch (int32)
-constexpr uint32_t kPoolStageBytes = 128 * kPoolPitch * 4;     // one staging tile (34 KB, 1 KB multiple)
+constexpr int kPoolRows = 7, kPoolCols = 3;  // pooled outputs per 16 x 8 conv tile (3x3/s2 windows)
+constexpr int kPoolPix = kPoolRows * kPoolCols;
+// Per epilogue set: the pooled int32 accumulators of one tile pair
+// ([tile][pooled pixel][64 channels]), staged for the vectorised epilogue.
+constexpr uint32_t kPoolStageBytes = ((2 * kPoolPix * 64 * 4) + 1023u) & ~1023u;
 
 struct EpiParams {
   void* out;
@@ -107,6 +110,9 @@ struct ConvParams {
   uint32_t halo_bytes;     // 1024-aligned bytes per halo stage
   uint32_t halo_tx_bytes;  // bytes the TMA loads of one stage deliver
   int slot_qh[4], slot_qw[4];  // per slot: TMA start offset in phase-view units
+  int wc_bytes;            // > 0: the halo map merges W and C (16-byte pixels, stride 1, one
+                           //    channel group) into one dimension, so one box row is a whole
+                           //    halo row; the TMA x coordinate is then pixel * wc_bytes
   int kb_per_group;
   uint32_t ab_off;         // smem offset of the epilogue's alpha / beta copies (0: read from global)
   int ab_pitch;            // floats from the alpha copy to the beta copy
@@ -117,7 +123,7 @@ struct ConvParams {
                            //    output row g / 2 of image 2 * tile + g % 2
   int n;                   // images
   int pho, pwo;            // pooled output size
-  uint32_t pool_off;       // smem offset of the int32 accumulator staging tile
+  uint32_t pool_off;       // pooled conv: smem offset of the per-set output staging (kPoolStageBytes each)
   uint32_t dtab_off;       // resident weights: smem offset of the MMA descriptor table
                            // ((A, B) pairs per halo stage, channel group and issued K-step)
   // A-operand descriptor of each 32-byte K-step relative to the halo stage
@@ -622,97 +628,135 @@ __device__ __forceinline__ bool row_coords(const KParams& p, int mt, int m, long
   }
 }
 
-// Fused 3x3/s2/p1 max pool of one conv tile (BN <= 64 channels): every
-// epilogue warp stages its int32 accumulators in smem and frees the TMEM
-// buffer; after a named barrier each thread reduces one (pooled pixel,
-// 4 channels) window over in-image conv pixels, keeping the max and the
-// min (the epilogue is increasing in acc where alpha >= 0, decreasing where
-// alpha < 0), applies the epilogue to the selected accumulator and stores
-// the pooled codes (out) and float32 values (aux).
-template <int BN, int kSetWarps>
-__device__ __forceinline__ void pool_epilogue(const KParams& p, const EpiConsts& k, uint32_t t_addr,
-                                              uint8_t* stage_bytes, const ConvTile& ct, int m, int slice, int slices,
-                                              int ew, int lane, uint64_t* tempty, int bar_id) {
-  int32_t* stg = reinterpret_cast<int32_t*>(stage_bytes);
-  for (int c0 = slice * (BN / slices); c0 < (slice + 1) * (BN / slices); c0 += 16) {
-    uint32_t acc[16];
-    tmem_ld16(t_addr + c0, acc);
-    tmem_ld_wait();
-    int4* dst = reinterpret_cast<int4*>(stg + m * kPoolPitch + c0);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      dst[i] = make_int4(int(acc[4 * i]), int(acc[4 * i + 1]), int(acc[4 * i + 2]), int(acc[4 * i + 3]));
-  }
-  tc_fence_before();
-  mbar_arrive(tempty);
-  bar_sync(bar_id, kSetWarps * 32);
+// Fused 3x3/s2/p1 max pool, channel-major accumulators. In the pooled
+// stem's M = 64 MMA the accumulator rows are output channels and the columns
+// the 128 conv pixels of a 16 x 8 tile (column = row * 8 + col), and each
+// TMEM buffer holds two tiles: tile 0 of the pair in lanes 0-15 of every
+// 32-lane quadrant, tile 1 in lanes 16-31. The thread of lane l in quadrant q
+// therefore owns channel 16 q + (l & 15) of tile (l >> 4) and pools it in
+// registers: per conv row, the max (or min) of the three columns of each
+// pooled column, then of the three rows of each pooled row. The epilogue is
+// increasing in acc where alpha >= 0 and decreasing where alpha < 0, so the
+// channel's alpha picks max or min (`use_max`) and the pooled accumulator is
+// the one the epilogue then maps. Conv pixels outside the image take the
+// value of their nearest in-image neighbour of the same window (the window
+// centre is always inside), which leaves max and min unchanged. The pooled
+// accumulators go to the set's staging area (sacc: [pooled pixel][64
+// channels] of this lane's tile). `valid` is false for the lanes of a missing
+// second tile; every lane still takes part in the warp-wide TMEM loads.
+__device__ __forceinline__ void pool_channel_tile(const KParams& p, uint32_t t_addr, const ConvTile& ct, bool valid,
+                                                  int ch, bool use_max, int* sacc) {
   const ConvParams& c = p.conv;
-  const EpiParams& e = p.epi;
-  const int img = ct.img, th = ct.th, tw = ct.tw;
-  const int oh0 = th * 2 * kPoolRows - 1, ow0 = tw * 2 * kPoolCols - 1;
-  constexpr int kQuads = BN / 4;
-  for (int w = ew * 32 + lane; w < kPoolRows * kPoolCols * kQuads; w += kSetWarps * 32) {
-    const int pix = w / kQuads, quad = w - pix * kQuads;
-    const int pr_l = pix / kPoolCols, pc_l = pix - pr_l * kPoolCols;
-    const int pr = th * kPoolRows + pr_l, pc = tw * kPoolCols + pc_l;
-    const int ch = quad * 4;
-    if (pr < c.pho && pc < c.pwo && ch < e.n_total) {
-      // Window rows / columns outside the image are clamped to the nearest
-      // inside one; the window centre is always inside, so a clamped index
-      // repeats an element of the same window and leaves max and min as they are.
-      int rr[3], cc[3];
+  const int oh0 = ct.th * (2 * kPoolRows) - 1, ow0 = ct.tw * (2 * kPoolCols) - 1;
+  const int right_from = c.wo - ow0;   // first tile column outside the image
+  const int bottom_from = c.ho - oh0;  // first tile row outside the image
+  // Max pooling of the negated accumulators gives the min: one code path.
+  const int sgn = use_max ? 0 : -1;
+  int ev[kPoolCols], od[kPoolCols];  // pooled-column values of the last even / odd row
 #pragma unroll
-      for (int d = 0; d < 3; ++d) {
-        rr[d] = min(max(2 * pr_l + d, -oh0), c.ho - 1 - oh0);
-        cc[d] = min(max(2 * pc_l + d, -ow0), c.wo - 1 - ow0);
+  for (int j = 0; j < kPoolCols; ++j) ev[j] = od[j] = 0;
+#pragma unroll
+  for (int i = 0; i < kTileH / 2; ++i) {
+    uint32_t v[16];
+    tmem_ld16(t_addr + 16 * i, v);
+    tmem_ld_wait();
+#pragma unroll
+    for (int s2 = 0; s2 < 2; ++s2) {
+      const int r = 2 * i + s2;
+      if (r > 2 * kPoolRows) break;  // rows 0 .. 14 feed the 7 pooled rows
+      int x[kTileW];
+#pragma unroll
+      for (int cc = 0; cc < kTileW; ++cc) x[cc] = (int(v[kTileW * s2 + cc]) ^ sgn) - sgn;
+      if (ow0 < 0) x[0] = x[1];
+      if (right_from < kTileW) {
+#pragma unroll
+        for (int cc = 1; cc < kTileW; ++cc)
+          if (cc >= right_from) x[cc] = x[cc - 1];
       }
-      // Row by row: max / min of the row's three pixels, then of the rows.
-      int mx[4], mn[4];
+      int hx[kPoolCols];
 #pragma unroll
-      for (int dy = 0; dy < 3; ++dy) {
-        const int* row = stg + rr[dy] * kTileW * kPoolPitch + ch;
-        const int4 v0 = *reinterpret_cast<const int4*>(row + cc[0] * kPoolPitch);
-        const int4 v1 = *reinterpret_cast<const int4*>(row + cc[1] * kPoolPitch);
-        const int4 v2 = *reinterpret_cast<const int4*>(row + cc[2] * kPoolPitch);
-        const int rmx[4] = {__vimax3_s32(v0.x, v1.x, v2.x), __vimax3_s32(v0.y, v1.y, v2.y),
-                            __vimax3_s32(v0.z, v1.z, v2.z), __vimax3_s32(v0.w, v1.w, v2.w)};
-        const int rmn[4] = {__vimin3_s32(v0.x, v1.x, v2.x), __vimin3_s32(v0.y, v1.y, v2.y),
-                            __vimin3_s32(v0.z, v1.z, v2.z), __vimin3_s32(v0.w, v1.w, v2.w)};
+      for (int j = 0; j < kPoolCols; ++j) hx[j] = __vimax3_s32(x[2 * j], x[2 * j + 1], x[2 * j + 2]);
+      if (r >= bottom_from) {  // below the image: repeat the row above
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          mx[i] = dy == 0 ? rmx[i] : max(mx[i], rmx[i]);
-          mn[i] = dy == 0 ? rmn[i] : min(mn[i], rmn[i]);
+        for (int j = 0; j < kPoolCols; ++j) hx[j] = (r & 1) ? ev[j] : od[j];
+      }
+      if (r & 1) {
+#pragma unroll
+        for (int j = 0; j < kPoolCols; ++j) {
+          if (r == 1 && oh0 < 0) ev[j] = hx[j];  // row 0 lies above the image: row 1 stands in for it
+          od[j] = hx[j];
         }
+        continue;
       }
-      float y[4];
-      int q[4];
+      if (r >= 2 && valid) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float a = e.alpha ? __ldg(e.alpha + ch + i) : e.alpha_scalar;
-        float v = __fmul_rn(__int2float_rn(a >= 0.0f ? mx[i] : mn[i]), a);
-        if (e.beta) v = __fadd_rn(v, __ldg(e.beta + ch + i));
-        if (e.relu) v = fmaxf(v, 0.0f);
-        y[i] = v;
-        q[i] = int(__float_as_int(__fadd_rn(fminf(fmaxf(lsq_guard(v, __fmul_rn(v, k.rs), e.out_scale), k.qnf),
-                                                    k.qpf), 12582912.0f)) - 0x4B400000);
+        for (int j = 0; j < kPoolCols; ++j)
+          sacc[((r / 2 - 1) * kPoolCols + j) * 64 + ch] = (__vimax3_s32(ev[j], od[j], hx[j]) ^ sgn) - sgn;
       }
-      const long long prow = ((long long)img * c.pho + pr) * c.pwo + pc;
-      if (e.aux) *reinterpret_cast<float4*>(e.aux + prow * e.aux_ld + ch) = make_float4(y[0], y[1], y[2], y[3]);
-      if (e.out_kind == 3) {
-        const uint32_t word = (uint32_t(q[0]) & 0xFFu) | ((uint32_t(q[1]) & 0xFFu) << 8) |
-                              ((uint32_t(q[2]) & 0xFFu) << 16) | ((uint32_t(q[3]) & 0xFFu) << 24);
-        *reinterpret_cast<uint32_t*>(static_cast<int8_t*>(e.out) + prow * e.s_pix + ch) = word;
-      } else if (e.out_kind == 1) {
-        *reinterpret_cast<float4*>(static_cast<float*>(e.out) + prow * e.s_pix + ch) =
-            make_float4(y[0], y[1], y[2], y[3]);
-      }
+#pragma unroll
+      for (int j = 0; j < kPoolCols; ++j) ev[j] = hx[j];
     }
   }
-  bar_sync(bar_id, kSetWarps * 32);  // the staging tile is free for the next tile
+}
+
+// Epilogue and stores of a staged tile pair. Thread tid takes channel quad
+// tid & 15 (alpha a4 / beta b4 are that quad's) of pooled pixels
+// (tid >> 4) + 8 i of both tiles: float32 values (aux, or out for float32
+// output) and int8 codes stored as one vector each.
+__device__ __forceinline__ void pool_store_pair(const KParams& p, const EpiConsts& k, const int* sacc,
+                                                const ConvTile& ct0, const ConvTile& ct1, bool has1, int tid,
+                                                float4 a4, float4 b4) {
+  const ConvParams& c = p.conv;
+  const EpiParams& e = p.epi;
+  const int quad = tid & 15;
+  if (4 * quad >= e.n_total) return;
+  const int ch = 4 * quad;
+#pragma unroll 1
+  for (int it = tid >> 4; it < (has1 ? 2 : 1) * kPoolPix; it += 8) {
+    const int h = it >= kPoolPix ? 1 : 0, px = it - h * kPoolPix;
+    const ConvTile& ct = h ? ct1 : ct0;
+    const int pr_l = px / kPoolCols, pc_l = px - pr_l * kPoolCols;
+    const int pr = ct.th * kPoolRows + pr_l, pc = ct.tw * kPoolCols + pc_l;
+    if (pr >= c.pho || pc >= c.pwo) continue;
+    const int4 acc = *reinterpret_cast<const int4*>(sacc + (h * kPoolPix + px) * 64 + ch);
+    float y[4] = {__fmul_rn(i2f_exact(acc.x), a4.x), __fmul_rn(i2f_exact(acc.y), a4.y),
+                  __fmul_rn(i2f_exact(acc.z), a4.z), __fmul_rn(i2f_exact(acc.w), a4.w)};
+    if (e.beta) {
+      y[0] = __fadd_rn(y[0], b4.x);
+      y[1] = __fadd_rn(y[1], b4.y);
+      y[2] = __fadd_rn(y[2], b4.z);
+      y[3] = __fadd_rn(y[3], b4.w);
+    }
+    if (e.relu) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) y[i] = fmaxf(y[i], 0.0f);
+    }
+    const long long prow = ((long long)ct.img * c.pho + pr) * c.pwo + pc;
+    const float4 yv = make_float4(y[0], y[1], y[2], y[3]);
+    if (e.aux) *reinterpret_cast<float4*>(e.aux + prow * e.aux_ld + ch) = yv;
+    if (e.out_kind == 3) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int q = int(__float_as_int(__fadd_rn(
+                          fminf(fmaxf(lsq_guard(y[i], __fmul_rn(y[i], k.rs), e.out_scale), k.qnf), k.qpf),
+                          12582912.0f))) -
+                      0x4B400000;
+        word |= (uint32_t(q) & 0xFFu) << (8 * i);
+      }
+      *reinterpret_cast<uint32_t*>(static_cast<int8_t*>(e.out) + prow * e.s_pix + ch) = word;
+    } else if (e.out_kind == 1) {
+      *reinterpret_cast<float4*>(static_cast<float*>(e.out) + prow * e.s_pix + ch) = yv;
+    }
+  }
 }
 
 // ------------------------------ kernel -------------------------------------
-template <int BN, bool kInt4, bool kConv>
+// kPool (conv, 8-bit weights, <= 64 channels, resident weights): the fused
+// 3x3/s2 max pool, on M = 64 MMAs with the weights as the A operand (rows =
+// output channels) and the tile's 128 conv pixels as B; two tiles share each
+// 128-column TMEM buffer (lanes 0-15 / 16-31 of every quadrant).
+template <int BN, bool kInt4, bool kConv, bool kPool = false>
 __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
     w4a8_mma_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                     const __grid_constant__ CUtensorMap tmH0, const __grid_constant__ CUtensorMap tmH1,
@@ -722,10 +766,12 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
   constexpr int kUnpackWarp0 = Roles<kConv>::kUnpackWarp0;
   constexpr int kUnpackThreads = Roles<kConv>::kUnpackWarps * 32;
   constexpr int kUnpackGroups = 2;  // unpack warp groups on alternate k-blocks
-  constexpr int kNB = acc_buffers(BN, kConv);        // accumulator buffers = epilogue warp sets
-  constexpr int kSetWarps = kEpiWarps / kNB;         // warps per set (a multiple of 4)
-  constexpr int kSlices = kSetWarps / 4;             // column slices per TMEM lane quadrant
-  constexpr uint32_t kTmemCols = tmem_columns(BN, kConv);
+  static_assert(!kPool || (kConv && BN == 64 && !kInt4), "the pooled conv: 8-bit weights, 64 channels");
+  constexpr int kNB = kPool ? 4 : acc_buffers(BN, kConv);  // accumulator buffers = epilogue warp sets
+  constexpr int kSetWarps = kEpiWarps / kNB;               // warps per set (a multiple of 4)
+  constexpr int kSlices = kSetWarps / 4;                   // column slices per TMEM lane quadrant
+  constexpr uint32_t kBufCols = kPool ? kBM : BN;          // TMEM columns per buffer (kPool: 128 pixels)
+  constexpr uint32_t kTmemCols = kPool ? 512u : tmem_columns(BN, kConv);
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_full[kMaxStages];
   __shared__ __align__(8) uint64_t bar_ready[kMaxStages];
@@ -840,6 +886,9 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
               if (pack2)  // map dims (c, group, W, N, H): both images' halo rows, interleaved
                 tma_load_5d(hdst + sl * slot_bytes, m, &bar_hfull[hs], 0, g, ow0 + p.conv.slot_qw[sl], 2 * ct.img,
                             oh0 + p.conv.slot_qh[sl]);
+              else if (p.conv.wc_bytes)  // map dims (W * C, 1, 1, H, N)
+                tma_load_5d(hdst + sl * slot_bytes, m, &bar_hfull[hs], (ow0 + p.conv.slot_qw[sl]) * p.conv.wc_bytes,
+                            0, 0, oh0 + p.conv.slot_qh[sl], ct.img);
               else
                 tma_load_5d(hdst + sl * slot_bytes, m, &bar_hfull[hs], 0, g, ow0 + p.conv.slot_qw[sl],
                             oh0 + p.conv.slot_qh[sl], ct.img);
@@ -931,7 +980,38 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       int hs = 0, buf = 0;
       uint32_t hph = 0, tph = 0;
       bool ok = true;
-      if (resident) {
+      if (kPool && resident) {
+        // Pooled stem: tiles t, t + 1 of the CTA's range go to one buffer, at
+        // TMEM lanes 0 and 16 (M = 64: 16 lanes of each quadrant per tile);
+        // operands swapped (A = weights, B = the tile's pixels).
+        constexpr uint32_t idesc64 = make_idesc_i8(64, kBM);
+        ok = warp_wait<true>(lane, &bar_bres, 0, &abort_flag);
+        for (int t = t_begin; ok && t < t_end; t += 2) {
+          if (!warp_wait<true>(lane, &bar_tempty[buf], tph ^ 1, &abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          for (int h = 0; h < 2 && t + h < t_end; ++h) {
+            const uint32_t d_tmem = tmem_base + buf * kBufCols + (uint32_t(16 * h) << 16);
+            for (int g = 0; g < groups; ++g) {
+              ok &= warp_wait<true>(lane, &bar_hfull[hs], hph, &abort_flag);
+              tc_fence_after();
+              const ulonglong2* e = dtab + (hs * groups + g) * gsteps;
+              ulonglong2 d = e[0];
+              ulonglong2 dn = e[gsteps > 1 ? 1 : 0];
+              mma_i8_ss_elect(d_tmem, d.y, d.x, idesc64, g != 0 ? 1u : 0u);
+              for (int j = 1; j < gsteps; ++j) {
+                d = dn;
+                dn = e[j + 1 < gsteps ? j + 1 : j];
+                mma_i8_ss_elect(d_tmem, d.y, d.x, idesc64, 1u);
+              }
+              mma_commit_elect(&bar_hempty[hs]);
+              if (++hs == hstages) { hs = 0; hph ^= 1; }
+            }
+          }
+          mma_commit_elect(&bar_tfull[buf]);
+          if (++buf == kNB) { buf = 0; tph ^= 1; }
+        }
+        mma_commit_elect(&bar_drain);
+      } else if (resident) {
         ok = warp_wait<true>(lane, kInt4 ? &bar_bready : &bar_bres, 0, &abort_flag);
         // The inner loops carry no break: a failed wait clears `ok` and sets
         // the CTA's abort flag (so every later wait gives up within a few
@@ -1044,6 +1124,53 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
         if (global_timer_ns() - w0 > kWaitLimitNs) { atomicOr(p.err, kErrTimeoutDrain); break; }
       if (!ok) atomicOr(p.err, kErrTimeoutMma);
     }
+  } else if (kPool && warp >= 4 && warp < 4 + kEpiWarps) {
+    // ------------------------- pooled epilogue -----------------------------
+    // Set `set` (one warp per TMEM quadrant) takes the tile pairs of buffer
+    // `set`: pairs t_begin + 2 (set + j kNB).
+    const int q = warp & 3, set = (warp - 4) / kSetWarps, half = lane >> 4;
+    const int ch = 16 * q + (lane & 15);
+    const bool ch_ok = ch < p.epi.n_total;
+    EpiConsts k;
+    k.rs = p.epi.out_kind == 3 ? __frcp_rn(p.epi.out_scale) : 1.0f;
+    k.qnf = float(p.epi.qn);
+    k.qpf = float(p.epi.qp);
+    k.relu_in_clamp = false;
+    const float alpha = p.epi.alpha ? (ch_ok ? __ldg(p.epi.alpha + ch) : 0.0f) : p.epi.alpha_scalar;
+    const bool use_max = alpha >= 0.0f;
+    // This thread's channel quad in the store phase (tid & 15 = lane & 15).
+    const int sq4 = 4 * (lane & 15);
+    float4 a4 = make_float4(p.epi.alpha_scalar, p.epi.alpha_scalar, p.epi.alpha_scalar, p.epi.alpha_scalar);
+    float4 b4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (sq4 < p.epi.n_total) {
+      if (p.epi.alpha) a4 = __ldg(reinterpret_cast<const float4*>(p.epi.alpha + sq4));
+      if (p.epi.beta) b4 = __ldg(reinterpret_cast<const float4*>(p.epi.beta + sq4));
+    }
+    const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(set) * kBufCols;
+    uint32_t tph = 0;
+    for (int t = t_begin + 2 * set; t < t_end; t += 2 * kNB, tph ^= 1) {
+      const int tt = t + half;  // this lane's tile
+      const bool has1 = t + 1 < t_end;
+      ConvTile ct0, ct1;
+      ct0.init(p, t);
+      ct1.init(p, has1 ? t + 1 : t);
+      const ConvTile& ct = half ? ct1 : ct0;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait_idle(&bar_tfull[set], tph, &abort_flag) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) atomicOr(p.err, kErrTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after();
+      int* stage = reinterpret_cast<int*>(base + p.conv.pool_off + uint32_t(set) * kPoolStageBytes);
+      pool_channel_tile(p, t_addr, ct, tt < t_end && ch_ok, ch, use_max, stage + half * kPoolPix * 64);
+      tc_fence_before();
+      mbar_arrive(&bar_tempty[set]);  // the accumulators are in registers / staging now
+      bar_sync(2 + set, kSetWarps * 32);
+      pool_store_pair(p, k, stage, ct0, ct1, has1, (warp - 4) % kSetWarps * 32 + lane, a4, b4);
+      bar_sync(2 + set, kSetWarps * 32);  // the staging area is free for the next pair
+    }
   } else if (warp >= 4 && warp < 4 + kEpiWarps) {
     // ----------------------------- epilogue --------------------------------
     const int q = warp & 3;
@@ -1089,7 +1216,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
         valid = ct.row(p, m, out_off, prow);
       else
         valid = row_coords<false>(p, mt, m, out_off, prow);
-      if (p.epi.residual && !(kConv && p.conv.pool) && valid) {
+      if (p.epi.residual && valid) {
         // The float32 identity rows of this thread's pixel are pulled into L2
         // while the MMA still works on the tile, so the epilogue's loads hit.
         const char* r = reinterpret_cast<const char*>(p.epi.residual + prow * p.epi.res_ld + nt * BN);
@@ -1105,19 +1232,6 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
         break;
       }
       tc_fence_after();
-      if constexpr (kConv && BN == 64 && !kInt4) {  // the fused pool: 8-bit weights, <= 64 channels
-        if (p.conv.pool) {
-          pool_epilogue<BN, kSetWarps>(p, k, tmem_base + (uint32_t(q * 32) << 16) + buf * BN,
-                                       base + p.conv.pool_off + set * kPoolStageBytes, ct, m, slice, kSlices,
-                                       (warp - 4) % kSetWarps, lane, &bar_tempty[buf], 2 + set);
-          if (contig) {
-            for (int i = 0; i < kNB; ++i) ct.next(p);
-          } else if (t + kNB * t_step < t_end) {
-            ct.init(p, t + kNB * t_step);
-          }
-          continue;
-        }
-      }
       const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + buf * BN;
 #pragma unroll 1
       for (int c0 = slice * (BN / kSlices); c0 < (slice + 1) * (BN / kSlices); c0 += 16) {

@@ -244,13 +244,17 @@ def test_lower_quantize_3x3_matches_oracle(cuda):
     assert_equal(got, orc.lower_quantize_3x3(x, 0.05, 2, 127, 46), "lowering qn>0")
 
 
-@pytest.mark.parametrize("h,w", [(30, 26), (29, 27)])
-def test_conv_fused_maxpool(cuda, h, w):
+@pytest.mark.parametrize("h,w,n,o", [(30, 26, 2, 64), (29, 27, 2, 64), (29, 27, 40, 64), (31, 25, 23, 40)])
+def test_conv_fused_maxpool(cuda, h, w, n, o):
     """Stem-style conv with the 3x3/s2/p1 max pool fused into the epilogue;
     alpha has both signs (pooling picks the max or min accumulator). Odd
-    sizes put the last pooled row / column's window partly outside the image."""
-    g = rng(21 + h)
-    n, c, o = 2, 16, 64
+    sizes put the last pooled row / column's window partly outside the image.
+    Two tiles share each accumulator buffer: with 2 images every CTA gets one
+    tile (a pair with its second half empty), with 40 and 23 images CTAs get
+    several tiles, odd and even counts; 40 output channels leave part of
+    the channel lanes idle."""
+    g = rng(21 + h + n)
+    c = 16
     xq = rand_i8(g, (n, h, w, c))
     wt = rand_i8(g, (o, 4, 4, c))
     alpha = g.uniform(1e-4, 1e-3, o).astype(np.float32)

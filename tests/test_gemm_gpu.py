@@ -149,7 +149,47 @@ def test_linear_op_matches_oracle(cuda):
         assert_close(got, want.astype(np.float32), 1e-3, "linear tolerance")
 
 
-@pytest.mark.parametrize("m", [1, 5, 37])
+# One or two tokens run on the TMA-fed GEMV: 16-row groups streamed through a
+# shared-memory ring in k-slices of up to 1 KB per row. The cases cover a
+# ragged last row group (N % 16), fewer groups than SMs, many groups per CTA,
+# rows of one slice, exactly one full slice, a short tail slice (1056-byte
+# rows), several slices, strided weight rows (ldw > K/2) and activations
+# (lda > K), and the largest K whose activations still leave four stages.
+GEMV_CASES = [
+    # m, n, k, ldw pad (bytes), lda pad
+    (1, 8, 64, 0, 0),
+    (2, 33, 128, 0, 0),
+    (1, 1000, 2048, 0, 0),
+    (2, 1000, 2112, 16, 64),
+    (1, 5000, 4096, 0, 0),
+    (2, 4100, 8192, 48, 16),
+    (1, 300, 65536, 0, 0),
+    (2, 40, 65536, 0, 0),
+]
+
+
+@pytest.mark.parametrize("m,n,k,wpad,apad", GEMV_CASES)
+def test_gemv_tma_bitexact(cuda, m, n, k, wpad, apad):
+    g = rng(5000 + m * 7 + n + k)
+    x = rand_i8(g, (m, k))
+    w = rand_i4(g, (n, k))
+    bp = orc.pack_int4(w)
+    want = orc.int4_int8_gemm(x, bp)
+    wbuf = torch.zeros((n, k // 2 + wpad), dtype=torch.uint8, device=cuda)
+    wbuf[:, : k // 2] = to_dev(bp, cuda)
+    abuf = torch.zeros((m, k + apad), dtype=torch.int8, device=cuda)
+    abuf[:, :k] = to_dev(x, cuda)
+    out = torch.full((m, n), -7, dtype=torch.int32, device=cuda)
+    epi = ext.make_epilogue(ext.OUT_S32)
+    ext._check(ext.lib().w4a8_gemm(abuf.data_ptr(), abuf.stride(0), wbuf.data_ptr(), wbuf.stride(0), ext.W_INT4, m,
+                                   n, k, ctypes.byref(epi), out.data_ptr(), out.stride(0),
+                                   torch.cuda.current_stream().cuda_stream), "w4a8_gemm")
+    torch.cuda.synchronize()
+    assert_equal(out, want, f"gemv {m}x{n}x{k}")
+    assert ext.device_error() == 0
+
+
+@pytest.mark.parametrize("m", [1, 2, 5, 37])
 def test_gemm_small_m_paths(cuda, m):
     """Small-M INT4 GEMMs: up to 8 tokens run on the CUDA-core GEMV (packed
     weights streamed into registers), 9..64 tokens split K across work units
