@@ -604,6 +604,9 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
       }
   cp.n_slots = ns;
   cp.halo_bytes = (cp.slot_bytes * ns + 1023u) & ~1023u;
+  // The pooled conv loads a tile pair into each halo stage.
+  cp.tile_halo_bytes = cp.halo_bytes;
+  if (g->pool) cp.halo_bytes *= 2;
   cp.halo_tx_bytes = uint32_t(ns * img_mult * cp.halo_w * cp.halo_h * cg);
   cp.kb_per_group = kbpg;
   cp.tail_steps = (taps * cg + 31) / 32 - (kbpg - 1) * (kBK / 32);
@@ -661,7 +664,8 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   // Resident weights also keep the MMA's descriptor table: one 16-byte (A, B)
   // pair per issued K-step, channel group and halo stage.
   const int gsteps = (kbpg - 1) * (kBK / 32) + cp.tail_steps;
-  const uint32_t tab_stage = uint32_t(groups * gsteps * 16);
+  if (g->pool && groups != 1) return W4A8_ERR_UNSUPPORTED;  // the pooled conv: one channel group
+  const uint32_t tab_stage = uint32_t((g->pool ? 2 : groups) * gsteps * 16);
   uint32_t dtab_bytes = 0;
   p.b_resident = 0;
   if (p.tiles_n == 1 && bres_bytes + 2 * (cp.halo_bytes + tab_stage) + 1024u <= uint32_t(budget)) {

@@ -107,7 +107,8 @@ struct ConvParams {
   uint32_t a_layout;       // operand layout of the halo: swizzle matching cg (none for 16)
   int halo_w, halo_h;      // sub-halo size in pixels
   uint32_t slot_bytes;     // bytes per sub-halo (1024-aligned)
-  uint32_t halo_bytes;     // 1024-aligned bytes per halo stage
+  uint32_t halo_bytes;     // 1024-aligned bytes per halo stage (pooled conv: a tile pair)
+  uint32_t tile_halo_bytes;  // pooled conv: offset of the pair's second tile in a halo stage
   uint32_t halo_tx_bytes;  // bytes the TMA loads of one stage deliver
   int slot_qh[4], slot_qw[4];  // per slot: TMA start offset in phase-view units
   int wc_bytes;            // > 0: the halo map merges W and C (16-byte pixels, stride 1, one
@@ -873,26 +874,43 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
         const uint32_t htx = p.conv.halo_tx_bytes, hbytes = p.conv.halo_bytes, slot_bytes = p.conv.slot_bytes;
         ConvTile ct;
         ct.init(p, t_begin);
-        for (int t = t_begin; ok && t < t_end; t += t_step, ct.advance(p, t, t_step)) {
-          const int oh0 = pool ? ct.th * (2 * kPoolRows) - 1 : ct.th * kTileH;
-          const int ow0 = pool ? ct.tw * (2 * kPoolCols) - 1 : ct.tw * kTileW;
+        // One tile's halo window (a 5-D box per stride phase) for channel group g.
+        auto issue_halo = [&](uint8_t* hdst, uint64_t* bar, const ConvTile& tc, int g) {
+          const int oh0 = pool ? tc.th * (2 * kPoolRows) - 1 : tc.th * kTileH;
+          const int ow0 = pool ? tc.tw * (2 * kPoolCols) - 1 : tc.tw * kTileW;
+          for (int sl = 0; sl < n_slots; ++sl) {
+            const CUtensorMap* m = sl == 0 ? &tmH0 : sl == 1 ? &tmH1 : sl == 2 ? &tmH2 : &tmH3;
+            if (pack2)  // map dims (c, group, W, N, H): both images' halo rows, interleaved
+              tma_load_5d(hdst + sl * slot_bytes, m, bar, 0, g, ow0 + p.conv.slot_qw[sl], 2 * tc.img,
+                          oh0 + p.conv.slot_qh[sl]);
+            else if (p.conv.wc_bytes)  // map dims (W * C, 1, 1, H, N)
+              tma_load_5d(hdst + sl * slot_bytes, m, bar, (ow0 + p.conv.slot_qw[sl]) * p.conv.wc_bytes, 0, 0,
+                          oh0 + p.conv.slot_qh[sl], tc.img);
+            else
+              tma_load_5d(hdst + sl * slot_bytes, m, bar, 0, g, ow0 + p.conv.slot_qw[sl], oh0 + p.conv.slot_qh[sl],
+                          tc.img);
+          }
+        };
+        if (kPool) {
+          // Pooled conv (one channel group, resident weights): a halo stage
+          // holds a tile pair, one barrier phase for both.
+          for (int t = t_begin; ok && t < t_end; t += 2) {
+            const int pair = t + 1 < t_end ? 2 : 1;
+            if (!mbar_wait_t<true>(&bar_hempty[hs], hph ^ 1, &abort_flag)) { ok = false; break; }
+            mbar_arrive_expect_tx(&bar_hfull[hs], htx * uint32_t(pair));
+            for (int h = 0; h < pair; ++h) {
+              issue_halo(base + p.h_off + hs * hbytes + h * p.conv.tile_halo_bytes, &bar_hfull[hs], ct, 0);
+              ct.next(p);
+            }
+            if (++hs == hstages) { hs = 0; hph ^= 1; }
+          }
+        }
+        for (int t = t_begin; !kPool && ok && t < t_end; t += t_step, ct.advance(p, t, t_step)) {
           int kb = 0;
           for (int g = 0; ok && g < groups; ++g) {
             if (!mbar_wait_t<true>(&bar_hempty[hs], hph ^ 1, &abort_flag)) { ok = false; break; }
             mbar_arrive_expect_tx(&bar_hfull[hs], htx);
-            uint8_t* hdst = base + p.h_off + hs * hbytes;
-            for (int sl = 0; sl < n_slots; ++sl) {
-              const CUtensorMap* m = sl == 0 ? &tmH0 : sl == 1 ? &tmH1 : sl == 2 ? &tmH2 : &tmH3;
-              if (pack2)  // map dims (c, group, W, N, H): both images' halo rows, interleaved
-                tma_load_5d(hdst + sl * slot_bytes, m, &bar_hfull[hs], 0, g, ow0 + p.conv.slot_qw[sl], 2 * ct.img,
-                            oh0 + p.conv.slot_qh[sl]);
-              else if (p.conv.wc_bytes)  // map dims (W * C, 1, 1, H, N)
-                tma_load_5d(hdst + sl * slot_bytes, m, &bar_hfull[hs], (ow0 + p.conv.slot_qw[sl]) * p.conv.wc_bytes,
-                            0, 0, oh0 + p.conv.slot_qh[sl], ct.img);
-              else
-                tma_load_5d(hdst + sl * slot_bytes, m, &bar_hfull[hs], 0, g, ow0 + p.conv.slot_qw[sl],
-                            oh0 + p.conv.slot_qh[sl], ct.img);
-            }
+            issue_halo(base + p.h_off + hs * hbytes, &bar_hfull[hs], ct, g);
             if (++hs == hstages) { hs = 0; hph ^= 1; }
             if (resident) continue;
             for (int i = 0; i < kbpg; ++i, ++kb) {
@@ -967,13 +985,17 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       const int gsteps = (kbpg - 1) * 4 + p.conv.tail_steps;
       ulonglong2* dtab = reinterpret_cast<ulonglong2*>(base + p.conv.dtab_off);
       if (resident) {
-        const int per_stage = groups * gsteps;
+        // Pooled conv: "groups" indexes the tile of the pair (one channel group).
+        const int per_stage = (kPool ? 2 : groups) * gsteps;
         for (int i = lane; i < hstages * per_stage; i += 32) {
           const int h = i / per_stage, r = i - h * per_stage, g = r / gsteps, j = r - g * gsteps;
-          const uint32_t halo_lo = (base_u32 + p.h_off + uint32_t(h) * p.conv.halo_bytes) >> 4;
+          const uint32_t halo_lo =
+              (base_u32 + p.h_off + uint32_t(h) * p.conv.halo_bytes + (kPool ? uint32_t(g) * p.conv.tile_halo_bytes : 0u)) >>
+              4;
           const uint32_t kb = uint32_t(g * kbpg + (j >> 2));
           dtab[i] = make_ulonglong2(p.conv.step_desc[j] + halo_lo,
-                                    sw128_tmpl + (b_stage0 + kb * b_step) + 2 * uint32_t(j & 3));
+                                    sw128_tmpl + (b_stage0 + (kPool ? uint32_t(j >> 2) : kb) * b_step) +
+                                        2 * uint32_t(j & 3));
         }
         __syncwarp();
       }
@@ -989,24 +1011,22 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
         for (int t = t_begin; ok && t < t_end; t += 2) {
           if (!warp_wait<true>(lane, &bar_tempty[buf], tph ^ 1, &abort_flag)) { ok = false; break; }
           tc_fence_after();
+          ok &= warp_wait<true>(lane, &bar_hfull[hs], hph, &abort_flag);
+          tc_fence_after();
           for (int h = 0; h < 2 && t + h < t_end; ++h) {
             const uint32_t d_tmem = tmem_base + buf * kBufCols + (uint32_t(16 * h) << 16);
-            for (int g = 0; g < groups; ++g) {
-              ok &= warp_wait<true>(lane, &bar_hfull[hs], hph, &abort_flag);
-              tc_fence_after();
-              const ulonglong2* e = dtab + (hs * groups + g) * gsteps;
-              ulonglong2 d = e[0];
-              ulonglong2 dn = e[gsteps > 1 ? 1 : 0];
-              mma_i8_ss_elect(d_tmem, d.y, d.x, idesc64, g != 0 ? 1u : 0u);
-              for (int j = 1; j < gsteps; ++j) {
-                d = dn;
-                dn = e[j + 1 < gsteps ? j + 1 : j];
-                mma_i8_ss_elect(d_tmem, d.y, d.x, idesc64, 1u);
-              }
-              mma_commit_elect(&bar_hempty[hs]);
-              if (++hs == hstages) { hs = 0; hph ^= 1; }
+            const ulonglong2* e = dtab + (hs * 2 + h) * gsteps;
+            ulonglong2 d = e[0];
+            ulonglong2 dn = e[gsteps > 1 ? 1 : 0];
+            mma_i8_ss_elect(d_tmem, d.y, d.x, idesc64, 0u);
+            for (int j = 1; j < gsteps; ++j) {
+              d = dn;
+              dn = e[j + 1 < gsteps ? j + 1 : j];
+              mma_i8_ss_elect(d_tmem, d.y, d.x, idesc64, 1u);
             }
           }
+          mma_commit_elect(&bar_hempty[hs]);
+          if (++hs == hstages) { hs = 0; hph ^= 1; }
           mma_commit_elect(&bar_tfull[buf]);
           if (++buf == kNB) { buf = 0; tph ^= 1; }
         }
