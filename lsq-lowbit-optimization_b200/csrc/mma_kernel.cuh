@@ -703,12 +703,16 @@ __device__ __forceinline__ void pool_channel_tile(const KParams& p, uint32_t t_a
 // Epilogue and stores of a staged tile pair. Thread tid takes channel quad
 // tid & 15 (alpha a4 / beta b4 are that quad's) of pooled pixels
 // (tid >> 4) + 8 i of both tiles: float32 values (aux, or out for float32
-// output) and int8 codes stored as one vector each.
+// output) and int8 codes stored as one vector each. The arithmetic is
+// epilogue16_fast's on float pairs (bit-identical to the scalar forms).
 __device__ __forceinline__ void pool_store_pair(const KParams& p, const EpiConsts& k, const int* sacc,
                                                 const ConvTile& ct0, const ConvTile& ct1, bool has1, int tid,
-                                                float4 a4, float4 b4) {
+                                                ulonglong2 a2, ulonglong2 b2) {
   const ConvParams& c = p.conv;
   const EpiParams& e = p.epi;
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const uint64_t magic2 = fpair(kMagic, kMagic), neg_magic2 = fpair(-kMagic, -kMagic);
+  const uint64_t rs2 = fpair(k.rs, k.rs);
   const int quad = tid & 15;
   if (4 * quad >= e.n_total) return;
   const int ch = 4 * quad;
@@ -720,34 +724,56 @@ __device__ __forceinline__ void pool_store_pair(const KParams& p, const EpiConst
     const int pr = ct.th * kPoolRows + pr_l, pc = ct.tw * kPoolCols + pc_l;
     if (pr >= c.pho || pc >= c.pwo) continue;
     const int4 acc = *reinterpret_cast<const int4*>(sacc + (h * kPoolPix + px) * 64 + ch);
-    float y[4] = {__fmul_rn(i2f_exact(acc.x), a4.x), __fmul_rn(i2f_exact(acc.y), a4.y),
-                  __fmul_rn(i2f_exact(acc.z), a4.z), __fmul_rn(i2f_exact(acc.w), a4.w)};
+    // Float pairs, as in epilogue16_fast: exact int32 -> float32 for |acc| < 2^22.
+    uint64_t y[2];
+    if (e.acc_fits_22) {
+      y[0] = add2(uint64_t(uint32_t(acc.x) + 0x4B400000u) | (uint64_t(uint32_t(acc.y) + 0x4B400000u) << 32), neg_magic2);
+      y[1] = add2(uint64_t(uint32_t(acc.z) + 0x4B400000u) | (uint64_t(uint32_t(acc.w) + 0x4B400000u) << 32), neg_magic2);
+    } else {
+      y[0] = fpair(i2f_exact(acc.x), i2f_exact(acc.y));
+      y[1] = fpair(i2f_exact(acc.z), i2f_exact(acc.w));
+    }
+    y[0] = mul2(y[0], a2.x);
+    y[1] = mul2(y[1], a2.y);
     if (e.beta) {
-      y[0] = __fadd_rn(y[0], b4.x);
-      y[1] = __fadd_rn(y[1], b4.y);
-      y[2] = __fadd_rn(y[2], b4.z);
-      y[3] = __fadd_rn(y[3], b4.w);
+      y[0] = add2(y[0], b2.x);
+      y[1] = add2(y[1], b2.y);
     }
     if (e.relu) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) y[i] = fmaxf(y[i], 0.0f);
+      y[0] = fpair(fmaxf(flo(y[0]), 0.0f), fmaxf(fhi(y[0]), 0.0f));
+      y[1] = fpair(fmaxf(flo(y[1]), 0.0f), fmaxf(fhi(y[1]), 0.0f));
     }
     const long long prow = ((long long)ct.img * c.pho + pr) * c.pwo + pc;
-    const float4 yv = make_float4(y[0], y[1], y[2], y[3]);
-    if (e.aux) *reinterpret_cast<float4*>(e.aux + prow * e.aux_ld + ch) = yv;
+    if (e.aux) *reinterpret_cast<ulonglong2*>(e.aux + prow * e.aux_ld + ch) = make_ulonglong2(y[0], y[1]);
     if (e.out_kind == 3) {
-      uint32_t word = 0;
+      // LSQ codes as in epilogue16_fast: t = y * fl(1/s), exact quotient near ties.
+      uint64_t t[2];
+      bool slow = false;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int q = int(__float_as_int(__fadd_rn(
-                          fminf(fmaxf(lsq_guard(y[i], __fmul_rn(y[i], k.rs), e.out_scale), k.qnf), k.qpf),
-                          12582912.0f))) -
-                      0x4B400000;
-        word |= (uint32_t(q) & 0xFFu) << (8 * i);
+      for (int j = 0; j < 2; ++j) {
+        t[j] = mul2(y[j], rs2);
+        const uint64_t rt = add2(add2(t[j], magic2), neg_magic2);
+        const uint64_t d = add2(t[j], rt ^ 0x8000000080000000ull);
+        slow |= fabsf(flo(d)) > 0.49975586f;
+        slow |= fabsf(fhi(d)) > 0.49975586f;
       }
-      *reinterpret_cast<uint32_t*>(static_cast<int8_t*>(e.out) + prow * e.s_pix + ch) = word;
+      if (slow) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          t[j] = fpair(lsq_guard(flo(y[j]), flo(t[j]), e.out_scale), lsq_guard(fhi(y[j]), fhi(t[j]), e.out_scale));
+      }
+      uint32_t b[4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint64_t cq = add2(fpair(fminf(fmaxf(flo(t[j]), k.qnf), k.qpf), fminf(fmaxf(fhi(t[j]), k.qnf), k.qpf)),
+                                 magic2);
+        b[2 * j] = uint32_t(cq);
+        b[2 * j + 1] = uint32_t(cq >> 32);
+      }
+      *reinterpret_cast<uint32_t*>(static_cast<int8_t*>(e.out) + prow * e.s_pix + ch) =
+          __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
     } else if (e.out_kind == 1) {
-      *reinterpret_cast<float4*>(static_cast<float*>(e.out) + prow * e.s_pix + ch) = yv;
+      *reinterpret_cast<ulonglong2*>(static_cast<float*>(e.out) + prow * e.s_pix + ch) = make_ulonglong2(y[0], y[1]);
     }
   }
 }
@@ -1008,10 +1034,14 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
         // operands swapped (A = weights, B = the tile's pixels).
         constexpr uint32_t idesc64 = make_idesc_i8(64, kBM);
         ok = warp_wait<true>(lane, &bar_bres, 0, &abort_flag);
+        // Software-pipelined: the next pair's buffer and halo waits run
+        // while the tensor core still works through this pair's queued MMAs,
+        // and this pair's commits follow them.
+        if (ok && t_begin < t_end) {
+          ok = warp_wait<true>(lane, &bar_tempty[buf], tph ^ 1, &abort_flag);
+          ok = ok && warp_wait<true>(lane, &bar_hfull[hs], hph, &abort_flag);
+        }
         for (int t = t_begin; ok && t < t_end; t += 2) {
-          if (!warp_wait<true>(lane, &bar_tempty[buf], tph ^ 1, &abort_flag)) { ok = false; break; }
-          tc_fence_after();
-          ok &= warp_wait<true>(lane, &bar_hfull[hs], hph, &abort_flag);
           tc_fence_after();
           for (int h = 0; h < 2 && t + h < t_end; ++h) {
             const uint32_t d_tmem = tmem_base + buf * kBufCols + (uint32_t(16 * h) << 16);
@@ -1025,10 +1055,20 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
               mma_i8_ss_elect(d_tmem, d.y, d.x, idesc64, 1u);
             }
           }
+          int nbuf = buf + 1, nhs = hs + 1;
+          uint32_t ntph = tph, nhph = hph;
+          if (nbuf == kNB) { nbuf = 0; ntph ^= 1; }
+          if (nhs == hstages) { nhs = 0; nhph ^= 1; }
+          if (t + 2 < t_end) {
+            ok &= warp_wait<true>(lane, &bar_tempty[nbuf], ntph ^ 1, &abort_flag);
+            ok &= warp_wait<true>(lane, &bar_hfull[nhs], nhph, &abort_flag);
+          }
           mma_commit_elect(&bar_hempty[hs]);
-          if (++hs == hstages) { hs = 0; hph ^= 1; }
           mma_commit_elect(&bar_tfull[buf]);
-          if (++buf == kNB) { buf = 0; tph ^= 1; }
+          buf = nbuf;
+          tph = ntph;
+          hs = nhs;
+          hph = nhph;
         }
         mma_commit_elect(&bar_drain);
       } else if (resident) {
@@ -1160,11 +1200,12 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
     const bool use_max = alpha >= 0.0f;
     // This thread's channel quad in the store phase (tid & 15 = lane & 15).
     const int sq4 = 4 * (lane & 15);
-    float4 a4 = make_float4(p.epi.alpha_scalar, p.epi.alpha_scalar, p.epi.alpha_scalar, p.epi.alpha_scalar);
-    float4 b4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    ulonglong2 a2 = make_ulonglong2(fpair(p.epi.alpha_scalar, p.epi.alpha_scalar),
+                                    fpair(p.epi.alpha_scalar, p.epi.alpha_scalar));
+    ulonglong2 b2 = make_ulonglong2(0ull, 0ull);
     if (sq4 < p.epi.n_total) {
-      if (p.epi.alpha) a4 = __ldg(reinterpret_cast<const float4*>(p.epi.alpha + sq4));
-      if (p.epi.beta) b4 = __ldg(reinterpret_cast<const float4*>(p.epi.beta + sq4));
+      if (p.epi.alpha) a2 = __ldg(reinterpret_cast<const ulonglong2*>(p.epi.alpha + sq4));
+      if (p.epi.beta) b2 = __ldg(reinterpret_cast<const ulonglong2*>(p.epi.beta + sq4));
     }
     const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(set) * kBufCols;
     uint32_t tph = 0;
@@ -1188,7 +1229,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       tc_fence_before();
       mbar_arrive(&bar_tempty[set]);  // the accumulators are in registers / staging now
       bar_sync(2 + set, kSetWarps * 32);
-      pool_store_pair(p, k, stage, ct0, ct1, has1, (warp - 4) % kSetWarps * 32 + lane, a4, b4);
+      pool_store_pair(p, k, stage, ct0, ct1, has1, (warp - 4) % kSetWarps * 32 + lane, a2, b2);
       bar_sync(2 + set, kSetWarps * 32);  // the staging area is free for the next pair
     }
   } else if (warp >= 4 && warp < 4 + kEpiWarps) {
