@@ -67,7 +67,10 @@ constexpr int kPoolRows = 7, kPoolCols = 3;  // pooled outputs per 16 x 8 conv t
 constexpr int kPoolPix = kPoolRows * kPoolCols;
 // Per epilogue set: the pooled int32 accumulators of one tile pair
 // ([tile][pooled pixel][64 channels]), staged for the vectorised epilogue.
-constexpr uint32_t kPoolStageBytes = ((2 * kPoolPix * 64 * 4) + 1023u) & ~1023u;
+// The second tile starts 16 words further on, so the two half-warps that
+// write one pixel row of each tile hit different banks.
+constexpr int kPoolTileWords = kPoolPix * 64 + 16;
+constexpr uint32_t kPoolStageBytes = ((2 * kPoolTileWords * 4) + 1023u) & ~1023u;
 
 struct EpiParams {
   void* out;
@@ -723,7 +726,7 @@ __device__ __forceinline__ void pool_store_pair(const KParams& p, const EpiConst
     const int pr_l = px / kPoolCols, pc_l = px - pr_l * kPoolCols;
     const int pr = ct.th * kPoolRows + pr_l, pc = ct.tw * kPoolCols + pc_l;
     if (pr >= c.pho || pc >= c.pwo) continue;
-    const int4 acc = *reinterpret_cast<const int4*>(sacc + (h * kPoolPix + px) * 64 + ch);
+    const int4 acc = *reinterpret_cast<const int4*>(sacc + h * kPoolTileWords + px * 64 + ch);
     // Float pairs, as in epilogue16_fast: exact int32 -> float32 for |acc| < 2^22.
     uint64_t y[2];
     if (e.acc_fits_22) {
@@ -1225,7 +1228,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       }
       tc_fence_after();
       int* stage = reinterpret_cast<int*>(base + p.conv.pool_off + uint32_t(set) * kPoolStageBytes);
-      pool_channel_tile(p, t_addr, ct, tt < t_end && ch_ok, ch, use_max, stage + half * kPoolPix * 64);
+      pool_channel_tile(p, t_addr, ct, tt < t_end && ch_ok, ch, use_max, stage + half * kPoolTileWords);
       tc_fence_before();
       mbar_arrive(&bar_tempty[set]);  // the accumulators are in registers / staging now
       bar_sync(2 + set, kSetWarps * 32);
