@@ -263,9 +263,48 @@ def small_m_gemm_hbm(device, hbm_gbs: float) -> list:
         ms = total / iters
         nbytes = w.numel() + a.numel() + c.numel() * 4
         gbs = nbytes / (ms * 1e-3) / 1e9
+        # The same calls replayed from a CUDA graph, each after the flush: the
+        # device time a GEMM adds to a stream of kernels, without the per-call
+        # launch and event overhead (an empty kernel timed alone with events
+        # measures about 6 us here). Graph of `reps` x (flush, GEMM) minus a
+        # graph of `reps` x flush, best of three replays each.
+        reps = 20
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            ext.gemm(a, w, ext.W_INT4, k, epi, c)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        g_both, g_flush = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_both):
+            for _ in range(reps):
+                flush.max()
+                ext.gemm(a, w, ext.W_INT4, k, epi, c)
+        with torch.cuda.graph(g_flush):
+            for _ in range(reps):
+                flush.max()
+
+        def replay_ms(graph):
+            best = float("inf")
+            for _ in range(3):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                graph.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                best = min(best, e0.elapsed_time(e1))
+            return best
+
+        ms_graph = (replay_ms(g_both) - replay_ms(g_flush)) / reps
+        del g_both, g_flush
+        gbs_graph = nbytes / (ms_graph * 1e-3) / 1e9 if ms_graph > 0 else None
         out.append({"shape_mnk": [m, n, k], "path": "gemv" if m <= 8 else "split-k",
                     "us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm_gbs, 4),
-                    "l2": "flushed before each call (256 MiB read)"})
+                    "us_in_graph": round(ms_graph * 1e3, 2),
+                    "hbm_frac_in_graph": round(gbs_graph / hbm_gbs, 4) if gbs_graph else None,
+                    "l2": "flushed before each call (256 MiB read)",
+                    "timing": "us: per call between CUDA events; us_in_graph: per call inside a CUDA graph "
+                              "of (flush, GEMM) pairs minus a graph of flushes"})
     return out
 
 

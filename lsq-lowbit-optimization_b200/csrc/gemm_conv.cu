@@ -670,6 +670,7 @@ extern "C" int w4a8_conv2d(const int8_t* x, const void* W, int w_kind, int64_t l
   p.b_resident = 0;
   if (p.tiles_n == 1 && bres_bytes + 2 * (cp.halo_bytes + tab_stage) + 1024u <= uint32_t(budget)) {
     p.b_resident = 1;
+    cp.extra_set = (bn == 64 && !g->pool) ? 1 : 0;  // the unpack warps drain a fifth buffer
     p.stages = 1;
     p.halo_stages = std::min<int>(kMaxHaloStages, (budget - 1024 - bres_bytes) / (cp.halo_bytes + tab_stage));
     dtab_bytes = (uint32_t(p.halo_stages) * tab_stage + 1023u) & ~1023u;

@@ -128,6 +128,7 @@ struct ConvParams {
   int n;                   // images
   int pho, pwo;            // pooled output size
   uint32_t pool_off;       // pooled conv: smem offset of the per-set output staging (kPoolStageBytes each)
+  int extra_set;           // 64-channel conv, resident weights: the unpack warps drain a fifth buffer
   uint32_t dtab_off;       // resident weights: smem offset of the MMA descriptor table
                            // ((A, B) pairs per halo stage, channel group and issued K-step)
   // A-operand descriptor of each 32-byte K-step relative to the halo stage
@@ -801,15 +802,21 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
   constexpr int kSetWarps = kEpiWarps / kNB;               // warps per set (a multiple of 4)
   constexpr int kSlices = kSetWarps / 4;                   // column slices per TMEM lane quadrant
   constexpr uint32_t kBufCols = kPool ? kBM : BN;          // TMEM columns per buffer (kPool: 128 pixels)
-  constexpr uint32_t kTmemCols = kPool ? 512u : tmem_columns(BN, kConv);
+  // 64-channel convs with resident weights: the four unpack warps (one per
+  // TMEM quadrant) are free once the weights are expanded (or from the start
+  // with 8-bit weights) and drain a fifth accumulator buffer.
+  constexpr bool kExtra = kConv && BN == 64 && !kPool;
+  static_assert(!kExtra || (kNB == 4 && Roles<kConv>::kUnpackWarps == 4), "fifth set: four unpack warps");
+  constexpr uint32_t kTmemCols = (kPool || kExtra) ? 512u : tmem_columns(BN, kConv);
+  const int nb = (kExtra && p.conv.extra_set) ? kNB + 1 : kNB;  // accumulator buffers in use
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_full[kMaxStages];
   __shared__ __align__(8) uint64_t bar_ready[kMaxStages];
   __shared__ __align__(8) uint64_t bar_empty[kMaxStages];
   __shared__ __align__(8) uint64_t bar_hfull[kMaxHaloStages];
   __shared__ __align__(8) uint64_t bar_hempty[kMaxHaloStages];
-  __shared__ __align__(8) uint64_t bar_tfull[4];
-  __shared__ __align__(8) uint64_t bar_tempty[4];
+  __shared__ __align__(8) uint64_t bar_tfull[5];
+  __shared__ __align__(8) uint64_t bar_tempty[5];
   __shared__ __align__(8) uint64_t bar_drain;
   __shared__ __align__(8) uint64_t bar_bres;    // resident weights landed
   __shared__ __align__(8) uint64_t bar_bready;  // resident weights unpacked
@@ -831,7 +838,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       mbar_init(&bar_hfull[s], 1);
       mbar_init(&bar_hempty[s], 1);
     }
-    for (int b = 0; b < kNB; ++b) {
+    for (int b = 0; b < nb; ++b) {
       mbar_init(&bar_tfull[b], 1);
       mbar_init(&bar_tempty[b], kSetWarps * 32);
     }
@@ -1104,7 +1111,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
             if (++hs == hstages) { hs = 0; hph ^= 1; }
           }
           mma_commit_elect(&bar_tfull[buf]);
-          if (++buf == kNB) { buf = 0; tph ^= 1; }
+          if (++buf == nb) { buf = 0; tph ^= 1; }
         }
         // Drain: all tcgen05 ops of this warp complete before TMEM is freed.
         mma_commit_elect(&bar_drain);
@@ -1235,89 +1242,10 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       pool_store_pair(p, k, stage, ct0, ct1, has1, (warp - 4) % kSetWarps * 32 + lane, a2, b2);
       bar_sync(2 + set, kSetWarps * 32);  // the staging area is free for the next pair
     }
-  } else if (warp >= 4 && warp < 4 + kEpiWarps) {
-    // ----------------------------- epilogue --------------------------------
-    const int q = warp & 3;
-    const int set = (warp - 4) / kSetWarps;          // this warp drains buffer `set`
-    const int slice = ((warp - 4) % kSetWarps) >> 2;
-    const int m = q * 32 + lane;
-    EpiConsts k;
-    k.rs = p.epi.out_kind == 3 ? __frcp_rn(p.epi.out_scale) : 1.0f;
-    k.qnf = float(p.epi.qn);
-    k.qpf = float(p.epi.qp);
-    k.relu_in_clamp = p.epi.out_kind == 3 && p.epi.qn >= 0 && p.epi.aux == nullptr;
-    // Conv: alpha / beta are copied into shared memory once; every 16-column
-    // chunk then reads them there instead of making a round trip to L2.
-    const float* sa = nullptr;
-    const float* sb = nullptr;
-    if (kConv && p.conv.ab_off) {
-      float* a_s = reinterpret_cast<float*>(base + p.conv.ab_off);
-      float* b_s = a_s + p.conv.ab_pitch;
-      for (int i = (warp - 4) * 32 + lane; i < p.epi.n_total; i += kEpiWarps * 32) {
-        if (p.epi.alpha) a_s[i] = p.epi.alpha[i];
-        if (p.epi.beta) b_s[i] = p.epi.beta[i];
-      }
-      bar_sync(8, kEpiWarps * 32);
-      sa = p.epi.alpha ? a_s : nullptr;
-      sb = p.epi.beta ? b_s : nullptr;
-    }
-    // This warp set takes every kNB-th tile of the CTA's sequence (buffer `set`).
-    const int buf = set;
-    uint32_t tph = 0;
-    ConvTile ct;
-    if (kConv && t_begin + set * t_step < t_end) ct.init(p, t_begin + set * t_step);
-    for (int t = t_begin + set * t_step; t < t_end; t += kNB * t_step, tph ^= 1) {
-      int mt = 0, nt = 0;
-      if constexpr (!kConv) {
-        mt = t / p.tiles_n;
-        nt = t - mt * p.tiles_n;
-      } else {
-        nt = ct.nt;
-      }
-      long long out_off = 0, prow = 0;
-      bool valid;
-      if constexpr (kConv)
-        valid = ct.row(p, m, out_off, prow);
-      else
-        valid = row_coords<false>(p, mt, m, out_off, prow);
-      if (p.epi.residual && valid) {
-        // The float32 identity rows of this thread's pixel are pulled into L2
-        // while the MMA still works on the tile, so the epilogue's loads hit.
-        const char* r = reinterpret_cast<const char*>(p.epi.residual + prow * p.epi.res_ld + nt * BN);
-        const int nbytes = 4 * min(BN, p.epi.n_total - nt * BN);
-        for (int off = slice * 128; off < nbytes; off += 128 * kSlices)
-          asm volatile("prefetch.global.L2 [%0];" ::"l"(r + off));
-      }
-      int ok = 1;
-      if (lane == 0) ok = mbar_wait_idle(&bar_tfull[buf], tph, &abort_flag) ? 1 : 0;
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) {
-        if (lane == 0) atomicOr(p.err, kErrTimeoutEpilogue);
-        break;
-      }
-      tc_fence_after();
-      const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + buf * BN;
-#pragma unroll 1
-      for (int c0 = slice * (BN / kSlices); c0 < (slice + 1) * (BN / kSlices); c0 += 16) {
-        uint32_t acc[16];
-        tmem_ld16(t_addr + c0, acc);
-        tmem_ld_wait();
-        if (valid) {
-          const int n = nt * BN + c0;
-          epilogue16<kConv>(p.epi, k, acc, n, out_off + (long long)n * p.epi.s_ch, prow, sa, sb);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&bar_tempty[buf]);
-      if constexpr (kConv) {
-        if (contig) {
-          for (int i = 0; i < kNB; ++i) ct.next(p);
-        } else if (t + kNB * t_step < t_end) {
-          ct.init(p, t + kNB * t_step);
-        }
-      }
-    }
-  } else if (warp >= kUnpackWarp0 && kInt4) {
+  } else if (warp >= 4) {
+    if (warp >= kUnpackWarp0) {
+      if constexpr (kInt4) {
+      // ------------------------------ unpack ---------------------------------
     // ------------------------------ unpack ---------------------------------
     // kUnpackGroups groups of warps take alternate k-blocks, so one group's
     // unpack latency (wait, read, expand, write, proxy fence) overlaps the
@@ -1390,6 +1318,93 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
     __syncwarp();
     if (resident && ok && lane == 0) mbar_arrive(&bar_bready);
     if (!ok && ut == 0) atomicOr(p.err, kErrTimeoutUnpack);
+      }
+    }
+    if (warp < 4 + kEpiWarps || nb > kNB) {
+    // ----------------------------- epilogue --------------------------------
+    // Warps 4 + 4 s .. 4 + 4 s + 3 form set s; with a fifth set the unpack
+    // warps (after the resident weights are expanded) are set kNB.
+    const int q = warp & 3;
+    const int set = (warp - 4) / kSetWarps;          // this warp drains buffer `set`
+    const int slice = ((warp - 4) % kSetWarps) >> 2;
+    const int m = q * 32 + lane;
+    EpiConsts k;
+    k.rs = p.epi.out_kind == 3 ? __frcp_rn(p.epi.out_scale) : 1.0f;
+    k.qnf = float(p.epi.qn);
+    k.qpf = float(p.epi.qp);
+    k.relu_in_clamp = p.epi.out_kind == 3 && p.epi.qn >= 0 && p.epi.aux == nullptr;
+    // Conv: alpha / beta are copied into shared memory once; every 16-column
+    // chunk then reads them there instead of making a round trip to L2.
+    const float* sa = nullptr;
+    const float* sb = nullptr;
+    if (kConv && p.conv.ab_off) {
+      float* a_s = reinterpret_cast<float*>(base + p.conv.ab_off);
+      float* b_s = a_s + p.conv.ab_pitch;
+      for (int i = (warp - 4) * 32 + lane; i < p.epi.n_total; i += nb * kSetWarps * 32) {
+        if (p.epi.alpha) a_s[i] = p.epi.alpha[i];
+        if (p.epi.beta) b_s[i] = p.epi.beta[i];
+      }
+      bar_sync(8, nb * kSetWarps * 32);
+      sa = p.epi.alpha ? a_s : nullptr;
+      sb = p.epi.beta ? b_s : nullptr;
+    }
+    // This warp set takes every nb-th tile of the CTA's sequence (buffer `set`).
+    const int buf = set;
+    uint32_t tph = 0;
+    ConvTile ct;
+    if (kConv && t_begin + set * t_step < t_end) ct.init(p, t_begin + set * t_step);
+    for (int t = t_begin + set * t_step; t < t_end; t += nb * t_step, tph ^= 1) {
+      int mt = 0, nt = 0;
+      if constexpr (!kConv) {
+        mt = t / p.tiles_n;
+        nt = t - mt * p.tiles_n;
+      } else {
+        nt = ct.nt;
+      }
+      long long out_off = 0, prow = 0;
+      bool valid;
+      if constexpr (kConv)
+        valid = ct.row(p, m, out_off, prow);
+      else
+        valid = row_coords<false>(p, mt, m, out_off, prow);
+      if (p.epi.residual && valid) {
+        // The float32 identity rows of this thread's pixel are pulled into L2
+        // while the MMA still works on the tile, so the epilogue's loads hit.
+        const char* r = reinterpret_cast<const char*>(p.epi.residual + prow * p.epi.res_ld + nt * BN);
+        const int nbytes = 4 * min(BN, p.epi.n_total - nt * BN);
+        for (int off = slice * 128; off < nbytes; off += 128 * kSlices)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(r + off));
+      }
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait_idle(&bar_tfull[buf], tph, &abort_flag) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) atomicOr(p.err, kErrTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (int c0 = slice * (BN / kSlices); c0 < (slice + 1) * (BN / kSlices); c0 += 16) {
+        uint32_t acc[16];
+        tmem_ld16(t_addr + c0, acc);
+        tmem_ld_wait();
+        if (valid) {
+          const int n = nt * BN + c0;
+          epilogue16<kConv>(p.epi, k, acc, n, out_off + (long long)n * p.epi.s_ch, prow, sa, sb);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bar_tempty[buf]);
+      if constexpr (kConv) {
+        if (contig) {
+          for (int i = 0; i < nb; ++i) ct.next(p);
+        } else if (t + nb * t_step < t_end) {
+          ct.init(p, t + nb * t_step);
+        }
+      }
+    }
+    }
   }
 
   tc_fence_before();
