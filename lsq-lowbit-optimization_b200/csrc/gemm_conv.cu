@@ -195,9 +195,26 @@ int launch_gemv_t(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int 
   if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return W4A8_ERR_LAUNCH;
   const int per_block = ROWS ? kGemvRows : 32;
-  kern<<<unsigned((N + per_block - 1) / per_block), kGemvWarps * 32, smem, st>>>(
-      A, lda, static_cast<const uint8_t*>(W), ldw, M, N, K, e);
+  const dim3 grid(unsigned((N + per_block - 1) / per_block), ROWS ? 1u : unsigned((M + MT - 1) / MT));
+  kern<<<grid, kGemvWarps * 32, smem, st>>>(A, lda, static_cast<const uint8_t*>(W), ldw, M, N, K, e);
   return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH;
+}
+
+#ifndef W4A8_GEMV_TOKENS_MACS
+#define W4A8_GEMV_TOKENS_MACS 1.5e8
+#endif
+// Small GEMMs with 9..128 tokens whose tensor-core tiles could not fill
+// half the GPU and whose multiply-adds take the CUDA cores a few
+// microseconds: 8-token groups of the lane-per-row GEMV. The tensor-core
+// path is latency-bound there (TMEM allocation, pipeline ramp and epilogue
+// of a handful of k-blocks per CTA). Measured in CUDA graphs, weights in L2:
+// 16x2048x2048 10.6 -> 7.7 us, 32x1024x1024 8.9 -> 6.5, 64x1024x2048
+// 12.2 -> 10.4, 128x512x512 7.8 -> 6.7; at 256 tokens (256x1000x512) the
+// token groups cost more than they save (9.8 -> 23.8 us), hence the limit.
+bool use_gemv_tokens(int M, int N, int K, int sms) {
+  if (M <= kGemvMaxTokens || M > 128 || K % 64 || gemv_smem_bytes(kGemvMaxTokens, K) > 200 * 1024) return false;
+  const long long tiles = (long long)((M + kBM - 1) / kBM) * ((N + 63) / 64);
+  return tiles < sms / 2 && double(M) * double(N) * double(K) <= W4A8_GEMV_TOKENS_MACS;
 }
 
 int gemv_w4(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K,
@@ -237,7 +254,7 @@ int splitk_plan(int M, int N, int K, int sms, int& bn, int& kb_per) {
 int gemm_w4(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K,
             const w4a8_epilogue* epi, void* C, int64_t ldc, int bn, int sms, int* ws, size_t ws_bytes,
             cudaStream_t stream) {
-  if (use_gemv(M, K)) return gemv_w4(A, lda, W, ldw, M, N, K, epi, C, ldc, stream);
+  if (use_gemv(M, K) || use_gemv_tokens(M, N, K, sms)) return gemv_w4(A, lda, W, ldw, M, N, K, epi, C, ldc, stream);
   int kb_per = 0, bn_split = bn;
   const int splits = ws ? splitk_plan(M, N, K, sms, bn_split, kb_per) : 0;
   if (splits && ws_bytes < size_t(M) * size_t(N) * 4) return W4A8_ERR_ARG;

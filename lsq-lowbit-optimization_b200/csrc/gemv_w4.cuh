@@ -15,7 +15,10 @@
 // Lane-per-row form (3..8 tokens): block = 32 output channels (one per lane) x
 // kGemvWarps warps, each warp a contiguous K range; the warps' partial sums
 // are added in shared memory and the fused epilogue (epilogue16) runs on
-// 16-channel chunks per token. The row-per-warp form below serves 1-2 tokens.
+// 16-channel chunks per token. More tokens (small GEMMs whose tensor-core
+// tiles could not fill the GPU) run as a second grid dimension of 8-token
+// groups: block (x, y) takes channels 32 x .. and tokens 8 y ... The
+// row-per-warp form below serves 1-2 tokens.
 #pragma once
 
 #include "mma_kernel.cuh"
@@ -40,6 +43,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32) w4a8_gemv_w4_kernel(const int
                                                                        int M, int N, int K,
                                                                        const __grid_constant__ EpiParams e) {
   extern __shared__ __align__(16) uint32_t gsm[];
+  const int t0 = int(blockIdx.y) * MT;  // this block's first token
+  X += (long long)t0 * ldx;
+  M = min(M - t0, MT);
   const int kw = K / 4;  // de-interleaved words per token
   uint32_t* xs = gsm;
   int* red = reinterpret_cast<int*>(xs + MT * kw);
@@ -124,7 +130,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) w4a8_gemv_w4_kernel(const int
 #pragma unroll
       for (int i = 0; i < 16; ++i) a16[i] = uint32_t(fin[t * 32 + h * 16 + i]);
       const int nc = blockIdx.x * 32 + h * 16;
-      epilogue16(e, k, a16, nc, (long long)t * e.s_pix + (long long)nc * e.s_ch, t);
+      epilogue16(e, k, a16, nc, (long long)(t0 + t) * e.s_pix + (long long)nc * e.s_ch, t0 + t);
     }
   }
 }
