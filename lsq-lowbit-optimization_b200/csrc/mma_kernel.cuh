@@ -1384,18 +1384,23 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
       }
       tc_fence_after();
       const uint32_t t_addr = tmem_base + (uint32_t(q * 32) << 16) + buf * BN;
+      const int c_end = (slice + 1) * (BN / kSlices);
 #pragma unroll 1
-      for (int c0 = slice * (BN / kSlices); c0 < (slice + 1) * (BN / kSlices); c0 += 16) {
+      for (int c0 = slice * (BN / kSlices); c0 < c_end; c0 += 16) {
         uint32_t acc[16];
         tmem_ld16(t_addr + c0, acc);
         tmem_ld_wait();
+        if (c0 + 16 >= c_end) {
+          // The last chunk is in registers: the buffer goes back to the MMA
+          // before this chunk's epilogue runs.
+          tc_fence_before();
+          mbar_arrive(&bar_tempty[buf]);
+        }
         if (valid) {
           const int n = nt * BN + c0;
           epilogue16<kConv>(p.epi, k, acc, n, out_off + (long long)n * p.epi.s_ch, prow, sa, sb);
         }
       }
-      tc_fence_before();
-      mbar_arrive(&bar_tempty[buf]);
       if constexpr (kConv) {
         if (contig) {
           for (int i = 0; i < nb; ++i) ct.next(p);
