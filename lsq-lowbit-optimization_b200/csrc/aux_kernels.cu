@@ -4,6 +4,7 @@
 // and round-half-to-even: q = clamp(rint(x / s), qn, qp).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "w4a8.h"
@@ -102,48 +103,91 @@ __device__ __forceinline__ int quant_rs(float x, float scale, float rs, float qn
 // Space-to-depth by 2 + quantise, vectorised: a thread makes output pixels
 // 2j and 2j + 1 of one row from six coalesced float4 loads (3 channels x 2
 // input rows, 4 consecutive columns each). Needs c == 3, cp == 16, w % 4 == 0
-// and a 16-byte aligned x.
-__global__ void __launch_bounds__(256) s2d_q3_vec_kernel(const float* __restrict__ x, int8_t* __restrict__ y, int n,
+// and a 16-byte aligned x. threadIdx.y picks an output row (image * ho + Y)
+// of the block and threadIdx.x the column pairs j of that row, so no index
+// needs a 64-bit division. The 24 values of a thread are quantised as 12
+// float pairs (add/mul.rn.f32x2, bit-identical to the scalar forms) as soon
+// as they are loaded; if any t lies within 2^-12 of a half-integer the
+// thread reloads its inputs and redoes them through quant_rs's exact path.
+// At most 51 registers (5 blocks of 256 per SM): the kernel is bound by the
+// loads it keeps in flight.
+__device__ __forceinline__ uint64_t s2d_pair(float lo, float hi) {
+  return uint64_t(__float_as_uint(lo)) | (uint64_t(__float_as_uint(hi)) << 32);
+}
+__device__ __forceinline__ uint64_t s2d_add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t s2d_mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+__global__ void __launch_bounds__(256, 5) s2d_q3_vec_kernel(const float* __restrict__ x, int8_t* __restrict__ y, int n,
                                                          int h, int w, float scale, float rs, int qn, int qp) {
   const int ho = h / 2, wq = w / 4;  // wq thread columns of two output pixels each
-  const long long total = (long long)n * ho * wq;
+  const int row = int(blockIdx.x * blockDim.y + threadIdx.y);
+  if (row >= n * ho) return;
+  const int img = row / ho, Y = row - img * ho;
   const float qnf = float(qn), qpf = float(qp);
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int j = int(i % wq);
-    const long long t = i / wq;
-    const int Y = int(t % ho);
-    const int img = int(t / ho);
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const uint64_t rs2 = s2d_pair(rs, rs), magic2 = s2d_pair(kMagic, kMagic), nmagic2 = s2d_pair(-kMagic, -kMagic);
+  const float* xr = x + ((long long)img * 3 * h + 2 * Y) * w;
+  int8_t* yr = y + ((long long)row * (w / 2)) * 16;
+  for (int j = threadIdx.x; j < wq; j += blockDim.x) {
     float4 v[3][2];
 #pragma unroll
     for (int cc = 0; cc < 3; ++cc)
 #pragma unroll
       for (int dy = 0; dy < 2; ++dy)
-        v[cc][dy] = __ldcs(reinterpret_cast<const float4*>(x + (((long long)img * 3 + cc) * h + 2 * Y + dy) * w) + j);
-    // Channel (dy * 2 + dx) * 3 + cc of pixel p (columns 4j + 2p + dx).
-    uint32_t out[2][4];
+        v[cc][dy] = __ldcs(reinterpret_cast<const float4*>(xr + ((long long)cc * h + dy) * w) + j);
+    // Pair k = (dy * 2 + dx) * 3 + cc holds channel k of output pixels 2j
+    // (low half, columns 4j + dx) and 2j + 1 (high half, columns 4j + 2 + dx).
+    uint32_t out[2][3] = {{0u, 0u, 0u}, {0u, 0u, 0u}};
+    bool slow = false;
 #pragma unroll
-    for (int pp = 0; pp < 2; ++pp) {
-      int q[12];
+    for (int dy = 0; dy < 2; ++dy)
+#pragma unroll
+      for (int dx = 0; dx < 2; ++dx)
+#pragma unroll
+        for (int cc = 0; cc < 3; ++cc) {
+          const float4& f = v[cc][dy];
+          const int k = (dy * 2 + dx) * 3 + cc;
+          const uint64_t t = s2d_mul2(s2d_pair(dx == 0 ? f.x : f.y, dx == 0 ? f.z : f.w), rs2);
+          const uint64_t rt = s2d_add2(s2d_add2(t, magic2), nmagic2);
+          const uint64_t d = s2d_add2(t, rt ^ 0x8000000080000000ull);  // t - rint(t)
+          slow |= fabsf(__uint_as_float(uint32_t(d))) > 0.49975586f;
+          slow |= fabsf(__uint_as_float(uint32_t(d >> 32))) > 0.49975586f;
+          const float c0 = fminf(fmaxf(__uint_as_float(uint32_t(t)), qnf), qpf);
+          const float c1 = fminf(fmaxf(__uint_as_float(uint32_t(t >> 32)), qnf), qpf);
+          const uint64_t r = s2d_add2(s2d_pair(c0, c1), magic2);
+          out[0][k / 4] |= (uint32_t(r) & 0xFFu) << (8 * (k % 4));
+          out[1][k / 4] |= (uint32_t(r >> 32) & 0xFFu) << (8 * (k % 4));
+        }
+    if (slow) {  // some t within 2^-12 of a half-integer: reload and redo the thread's values exactly
+#pragma unroll
+      for (int pp = 0; pp < 2; ++pp)
+#pragma unroll
+        for (int wd = 0; wd < 3; ++wd) out[pp][wd] = 0u;
 #pragma unroll
       for (int dy = 0; dy < 2; ++dy)
 #pragma unroll
         for (int dx = 0; dx < 2; ++dx)
 #pragma unroll
           for (int cc = 0; cc < 3; ++cc) {
-            const float4& f = v[cc][dy];
-            const float e = pp == 0 ? (dx == 0 ? f.x : f.y) : (dx == 0 ? f.z : f.w);
-            q[(dy * 2 + dx) * 3 + cc] = quant_rs(e, scale, rs, qnf, qpf);
+            const float4 f = reinterpret_cast<const float4*>(xr + ((long long)cc * h + dy) * w)[j];
+            const int k = (dy * 2 + dx) * 3 + cc;
+            const int q0 = quant_rs(dx == 0 ? f.x : f.y, scale, rs, qnf, qpf);
+            const int q1 = quant_rs(dx == 0 ? f.z : f.w, scale, rs, qnf, qpf);
+            out[0][k / 4] |= (uint32_t(q0) & 0xFFu) << (8 * (k % 4));
+            out[1][k / 4] |= (uint32_t(q1) & 0xFFu) << (8 * (k % 4));
           }
-#pragma unroll
-      for (int wd = 0; wd < 3; ++wd)
-        out[pp][wd] = (uint32_t(q[4 * wd]) & 0xFFu) | ((uint32_t(q[4 * wd + 1]) & 0xFFu) << 8) |
-                      ((uint32_t(q[4 * wd + 2]) & 0xFFu) << 16) | ((uint32_t(q[4 * wd + 3]) & 0xFFu) << 24);
-      out[pp][3] = 0;
     }
-    uint4* dst = reinterpret_cast<uint4*>(y + (((long long)img * ho + Y) * (w / 2) + 2 * j) * 16);
-    dst[0] = make_uint4(out[0][0], out[0][1], out[0][2], out[0][3]);
-    dst[1] = make_uint4(out[1][0], out[1][1], out[1][2], out[1][3]);
+    uint4* dst = reinterpret_cast<uint4*>(yr + (2 * j) * 16);
+    dst[0] = make_uint4(out[0][0], out[0][1], out[0][2], 0u);
+    dst[1] = make_uint4(out[1][0], out[1][1], out[1][2], 0u);
   }
 }
 
@@ -293,10 +337,13 @@ extern "C" int w4a8_s2d_quantize(const float* x, int8_t* y, int n, int c, int h,
   if (!x || !y) return W4A8_ERR_ARG;
   if (reinterpret_cast<uintptr_t>(y) & 15) return W4A8_ERR_ALIGN;
   const long long total = (long long)n * (h / 2) * (w / 2);
-  if (c == 3 && c_pad == 16 && w % 4 == 0 && h % 2 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
-    const long long threads = (long long)n * (h / 2) * (w / 4);
+  const long long rows = (long long)n * (h / 2);
+  if (c == 3 && c_pad == 16 && w % 4 == 0 && h % 2 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      rows < (1ll << 31) - 4) {
     const float rs = 1.0f / scale;  // IEEE single division on the host: fl(1/s), as the guard band assumes
-    s2d_q3_vec_kernel<<<grid_for(threads, 256), 256, 0, (cudaStream_t)stream>>>(x, y, n, h, w, scale, rs, qn, qp);
+    const int bx = std::min(w / 4, 128), by = std::max(1, 256 / bx);  // whole rows of column pairs per block
+    s2d_q3_vec_kernel<<<unsigned((rows + by - 1) / by), dim3(bx, by), 0, (cudaStream_t)stream>>>(x, y, n, h, w, scale,
+                                                                                               rs, qn, qp);
     return finish();
   }
   s2d_q_kernel<<<grid_for(total, 128), 128, 0, (cudaStream_t)stream>>>(x, y, n, c, h, w, c_pad, scale, qn, qp);
