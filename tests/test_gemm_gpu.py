@@ -165,6 +165,9 @@ GEMV_CASES = [
     (2, 4100, 8192, 48, 16),
     (1, 300, 65536, 0, 0),
     (2, 40, 65536, 0, 0),
+    (1, 40000, 1024, 0, 0),  # 17 units of 16 rows per block, one 512-byte segment per row
+    (2, 3000, 3072, 32, 0),
+    (1, 24, 1024, 0, 0),  # fewer segments than warps
 ]
 
 
