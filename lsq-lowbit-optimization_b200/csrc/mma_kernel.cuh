@@ -661,13 +661,16 @@ __device__ __forceinline__ void pool_channel_tile(const KParams& p, uint32_t t_a
 #pragma unroll
   for (int j = 0; j < kPoolCols; ++j) ev[j] = od[j] = 0;
 #pragma unroll
-  for (int i = 0; i < kTileH / 2; ++i) {
-    uint32_t v[16];
-    tmem_ld16(t_addr + 16 * i, v);
+  for (int i2 = 0; i2 < kTileH / 4; ++i2) {  // four conv rows (two 16-column loads) per TMEM wait
+    uint32_t va[16], vb[16];
+    tmem_ld16(t_addr + 32 * i2, va);
+    tmem_ld16(t_addr + 32 * i2 + 16, vb);
     tmem_ld_wait();
 #pragma unroll
-    for (int s2 = 0; s2 < 2; ++s2) {
-      const int r = 2 * i + s2;
+    for (int s4 = 0; s4 < 4; ++s4) {
+      const uint32_t* v = s4 < 2 ? va : vb;
+      const int s2 = s4 & 1;
+      const int r = 4 * i2 + s4;
       if (r > 2 * kPoolRows) break;  // rows 0 .. 14 feed the 7 pooled rows
       int x[kTileW];
 #pragma unroll
