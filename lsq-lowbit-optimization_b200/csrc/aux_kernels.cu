@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <cstdint>
 
+#include "launch.cuh"
 #include "w4a8.h"
 
 namespace {
@@ -26,6 +27,8 @@ bool q_ok(float scale, int qn, int qp) { return scale > 0.0f && qn >= -128 && qp
 
 __global__ void quantize_rows_kernel(const float* __restrict__ x, long long ldx, int8_t* __restrict__ q,
                                      long long ldq, long long rows, int cols, float scale, int qn, int qp) {
+  w4a8::pdl_trigger();
+  w4a8::pdl_wait();
   const long long total = rows * ldq;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -39,6 +42,8 @@ __global__ void quantize_rows_kernel(const float* __restrict__ x, long long ldx,
 // tile of one image through shared memory.
 __global__ void nchw_to_nhwc_q_kernel(const float* __restrict__ x, int8_t* __restrict__ y, int c, int hw,
                                       int cp, float scale, int qn, int qp) {
+  w4a8::pdl_trigger();
+  w4a8::pdl_wait();
   __shared__ int8_t tile[32][33];
   const int img = blockIdx.z;
   const int c0 = blockIdx.y * 32;
@@ -61,6 +66,8 @@ __global__ void nchw_to_nhwc_q_kernel(const float* __restrict__ x, int8_t* __res
 // Space-to-depth by 2 + quantise: one thread per output pixel.
 __global__ void s2d_q_kernel(const float* __restrict__ x, int8_t* __restrict__ y, int n, int c, int h, int w,
                              int cp, float scale, int qn, int qp) {
+  w4a8::pdl_trigger();
+  w4a8::pdl_wait();
   const int ho = h / 2, wo = w / 2;
   const long long total = (long long)n * ho * wo;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -127,6 +134,8 @@ __device__ __forceinline__ uint64_t s2d_mul2(uint64_t a, uint64_t b) {
 
 __global__ void __launch_bounds__(256, 5) s2d_q3_vec_kernel(const float* __restrict__ x, int8_t* __restrict__ y, int n,
                                                          int h, int w, float scale, float rs, int qn, int qp) {
+  w4a8::pdl_trigger();
+  w4a8::pdl_wait();
   const int ho = h / 2, wq = w / 4;  // wq thread columns of two output pixels each
   const int row = int(blockIdx.x * blockDim.y + threadIdx.y);
   if (row >= n * ho) return;
@@ -195,6 +204,8 @@ __global__ void __launch_bounds__(256, 5) s2d_q3_vec_kernel(const float* __restr
 // taps quantise 0.0, columns >= c*9 are 0.
 __global__ void lower_q3x3_kernel(const float* __restrict__ x, int8_t* __restrict__ cols, int n, int c, int h,
                                   int w, int padded_k, float scale, int qn, int qp) {
+  w4a8::pdl_trigger();
+  w4a8::pdl_wait();
   const long long total = (long long)n * h * w * padded_k;
   const int kpr = c * 9;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -224,6 +235,8 @@ __device__ __forceinline__ uint32_t nibble_at(const uint8_t* row, long long k) {
 // One thread per output byte (two nibbles) of the reordered weights.
 __global__ void repack_kernel(const uint8_t* __restrict__ w_in, long long ld_in, int o, int c, int kh, int kw,
                               uint8_t* __restrict__ w_out, long long ld_out, int cp) {
+  w4a8::pdl_trigger();
+  w4a8::pdl_wait();
   const int taps = kh * kw;
   const int cg = cp < 128 ? cp : 128;
   const long long k_out = (long long)taps * cp;
@@ -249,6 +262,8 @@ __global__ void repack_kernel(const uint8_t* __restrict__ w_in, long long ld_in,
 // NHWC fp32 3x3/s2/p1 max pooling; one thread per (pixel, 4 channels).
 __global__ void maxpool_kernel(const float* __restrict__ x, float* __restrict__ yf, int8_t* __restrict__ yq,
                                int n, int h, int w, int c, int ho, int wo, float scale, int qn, int qp) {
+  w4a8::pdl_trigger();
+  w4a8::pdl_wait();
   const int c4 = c / 4;
   const long long total = (long long)n * ho * wo * c4;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
@@ -286,6 +301,8 @@ __global__ void maxpool_kernel(const float* __restrict__ x, float* __restrict__ 
 // Mean over hw (sequential float32 sum in (h, w) order, then / hw) + quantise.
 __global__ void avgpool_q_kernel(const float* __restrict__ x, int8_t* __restrict__ q, long long ldq, int n, int hw,
                                  int c, float scale, int qn, int qp) {
+  w4a8::pdl_trigger();
+  w4a8::pdl_wait();
   const long long total = (long long)n * c;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
@@ -304,6 +321,15 @@ __global__ void avgpool_q_kernel(const float* __restrict__ x, int8_t* __restrict
 
 int finish() { return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH; }
 
+// Every helper kernel goes out with programmatic dependent launch, like the
+// tensor-core kernels: it starts early and waits (pdl_wait, its first
+// statement) for the kernel ahead of it in the stream.
+template <typename... Exp, typename... Act>
+int launch(void (*kern)(Exp...), dim3 grid, dim3 block, cudaStream_t st, Act&&... args) {
+  if (w4a8::launch_kernel(kern, grid, block, 0, st, std::forward<Act>(args)...) != cudaSuccess) return W4A8_ERR_LAUNCH;
+  return finish();
+}
+
 }  // namespace
 
 extern "C" int w4a8_quantize_rows(const float* x, int64_t ldx, int8_t* q, int64_t ldq, int64_t rows, int cols,
@@ -311,9 +337,8 @@ extern "C" int w4a8_quantize_rows(const float* x, int64_t ldx, int8_t* q, int64_
   if (rows < 0 || cols < 0 || ldx < cols || ldq < cols || !q_ok(scale, qn, qp)) return W4A8_ERR_ARG;
   if (rows == 0 || ldq == 0) return W4A8_OK;
   if (!x || !q) return W4A8_ERR_ARG;
-  quantize_rows_kernel<<<grid_for(rows * ldq, 256), 256, 0, (cudaStream_t)stream>>>(x, ldx, q, ldq, rows, cols,
-                                                                                     scale, qn, qp);
-  return finish();
+  return launch(quantize_rows_kernel, dim3(grid_for(rows * ldq, 256)), dim3(256), (cudaStream_t)stream,
+                x, ldx, q, ldq, rows, cols, scale, qn, qp);
 }
 
 extern "C" int w4a8_quantize_nchw_to_nhwc(const float* x, int8_t* y, int n, int c, int h, int w, int c_pad,
@@ -324,8 +349,8 @@ extern "C" int w4a8_quantize_nchw_to_nhwc(const float* x, int8_t* y, int n, int 
   if (n > 65535) return W4A8_ERR_UNSUPPORTED;
   const int hw = h * w;
   dim3 grid((hw + 31) / 32, (c_pad + 31) / 32, n);
-  nchw_to_nhwc_q_kernel<<<grid, dim3(32, 8), 0, (cudaStream_t)stream>>>(x, y, c, hw, c_pad, scale, qn, qp);
-  return finish();
+  return launch(nchw_to_nhwc_q_kernel, dim3(grid), dim3(32, 8), (cudaStream_t)stream,
+                x, y, c, hw, c_pad, scale, qn, qp);
 }
 
 extern "C" int w4a8_s2d_quantize(const float* x, int8_t* y, int n, int c, int h, int w, int c_pad, float scale,
@@ -342,12 +367,11 @@ extern "C" int w4a8_s2d_quantize(const float* x, int8_t* y, int n, int c, int h,
       rows < (1ll << 31) - 4) {
     const float rs = 1.0f / scale;  // IEEE single division on the host: fl(1/s), as the guard band assumes
     const int bx = std::min(w / 4, 128), by = std::max(1, 256 / bx);  // whole rows of column pairs per block
-    s2d_q3_vec_kernel<<<unsigned((rows + by - 1) / by), dim3(bx, by), 0, (cudaStream_t)stream>>>(x, y, n, h, w, scale,
-                                                                                               rs, qn, qp);
-    return finish();
+    return launch(s2d_q3_vec_kernel, dim3(unsigned((rows + by - 1) / by)), dim3(bx, by), (cudaStream_t)stream,
+                  x, y, n, h, w, scale, rs, qn, qp);
   }
-  s2d_q_kernel<<<grid_for(total, 128), 128, 0, (cudaStream_t)stream>>>(x, y, n, c, h, w, c_pad, scale, qn, qp);
-  return finish();
+  return launch(s2d_q_kernel, dim3(grid_for(total, 128)), dim3(128), (cudaStream_t)stream,
+                x, y, n, c, h, w, c_pad, scale, qn, qp);
 }
 
 extern "C" int w4a8_lower_quantize_3x3(const float* x, int8_t* cols, int n, int c, int h, int w, int padded_k,
@@ -356,9 +380,8 @@ extern "C" int w4a8_lower_quantize_3x3(const float* x, int8_t* cols, int n, int 
   const long long total = (long long)n * h * w * padded_k;
   if (total == 0) return W4A8_OK;
   if (!x || !cols) return W4A8_ERR_ARG;
-  lower_q3x3_kernel<<<grid_for(total, 256), 256, 0, (cudaStream_t)stream>>>(x, cols, n, c, h, w, padded_k, scale,
-                                                                            qn, qp);
-  return finish();
+  return launch(lower_q3x3_kernel, dim3(grid_for(total, 256)), dim3(256), (cudaStream_t)stream,
+                x, cols, n, c, h, w, padded_k, scale, qn, qp);
 }
 
 extern "C" int w4a8_repack_oihw_int4(const uint8_t* w_in, int64_t ld_in, int o, int c, int kh, int kw,
@@ -369,9 +392,8 @@ extern "C" int w4a8_repack_oihw_int4(const uint8_t* w_in, int64_t ld_in, int o, 
   if (o == 0) return W4A8_OK;
   if (!w_in || !w_out) return W4A8_ERR_ARG;
   const long long total = (long long)o * ld_out;
-  repack_kernel<<<grid_for(total, 256), 256, 0, (cudaStream_t)stream>>>(w_in, ld_in, o, c, kh, kw, w_out, ld_out,
-                                                                        c_pad);
-  return finish();
+  return launch(repack_kernel, dim3(grid_for(total, 256)), dim3(256), (cudaStream_t)stream,
+                w_in, ld_in, o, c, kh, kw, w_out, ld_out, c_pad);
 }
 
 extern "C" int w4a8_maxpool3x3s2(const float* x_f, float* y_f, int8_t* y_q, int n, int h, int w, int c, int ho,
@@ -385,9 +407,8 @@ extern "C" int w4a8_maxpool3x3s2(const float* x_f, float* y_f, int8_t* y_q, int 
       (reinterpret_cast<uintptr_t>(y_q) & 3))
     return W4A8_ERR_ALIGN;
   const long long total = (long long)n * ho * wo * (c / 4);
-  maxpool_kernel<<<grid_for(total, 256), 256, 0, (cudaStream_t)stream>>>(x_f, y_f, y_q, n, h, w, c, ho, wo, scale,
-                                                                         qn, qp);
-  return finish();
+  return launch(maxpool_kernel, dim3(grid_for(total, 256)), dim3(256), (cudaStream_t)stream,
+                x_f, y_f, y_q, n, h, w, c, ho, wo, scale, qn, qp);
 }
 
 extern "C" int w4a8_avgpool_quantize(const float* x, int8_t* q, int64_t ldq, int n, int hw, int c, float scale,
@@ -395,7 +416,6 @@ extern "C" int w4a8_avgpool_quantize(const float* x, int8_t* q, int64_t ldq, int
   if (n < 0 || hw < 1 || c < 1 || ldq < c || !q_ok(scale, qn, qp)) return W4A8_ERR_ARG;
   if (n == 0) return W4A8_OK;
   if (!x || !q) return W4A8_ERR_ARG;
-  avgpool_q_kernel<<<grid_for((long long)n * c, 256), 256, 0, (cudaStream_t)stream>>>(x, q, ldq, n, hw, c, scale,
-                                                                                      qn, qp);
-  return finish();
+  return launch(avgpool_q_kernel, dim3(grid_for((long long)n * c, 256)), dim3(256), (cudaStream_t)stream,
+                x, q, ldq, n, hw, c, scale, qn, qp);
 }

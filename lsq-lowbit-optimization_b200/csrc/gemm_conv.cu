@@ -4,6 +4,7 @@
 
 #include "gemm_w4_kernel.cuh"
 #include "gemv_w4.cuh"
+#include "launch.cuh"
 #include "mma_kernel.cuh"
 #include "tensormap.cuh"
 
@@ -39,7 +40,9 @@ int launch_t(const CUtensorMap& tA, const CUtensorMap& tW, const CUtensorMap* tH
       return W4A8_ERR_LAUNCH;
     attr_done.set(dev, true);
   }
-  kern<<<grid, Roles<CV>::kThreads, kSmemAttr, st>>>(tA, tW, tH[0], tH[1], tH[2], tH[3], p);
+  if (launch_kernel(kern, dim3(unsigned(grid)), dim3(Roles<CV>::kThreads), kSmemAttr, st, tA, tW, tH[0], tH[1], tH[2],
+                    tH[3], p) != cudaSuccess)
+    return W4A8_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH;
 }
 
@@ -72,7 +75,8 @@ int launch_w4_t(const CUtensorMap& tA, const CUtensorMap& tW, const KParams& p, 
     if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) return 0;
     return clusters;
   }
-  if (cudaLaunchKernelEx(&cfg, kern, tA, tW, p) != cudaSuccess) return W4A8_ERR_LAUNCH;
+  if (launch_kernel_attrs(kern, cfg.gridDim, cfg.blockDim, kSmemAttr, st, attr, 1, tA, tW, p) != cudaSuccess)
+    return W4A8_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH;
 }
 
@@ -196,7 +200,9 @@ int launch_gemv_t(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int 
     return W4A8_ERR_LAUNCH;
   const int per_block = ROWS ? kGemvRows : 32;
   const dim3 grid(unsigned((N + per_block - 1) / per_block), ROWS ? 1u : unsigned((M + MT - 1) / MT));
-  kern<<<grid, kGemvWarps * 32, smem, st>>>(A, lda, static_cast<const uint8_t*>(W), ldw, M, N, K, e);
+  if (launch_kernel(kern, grid, dim3(kGemvWarps * 32), smem, st, A, lda, static_cast<const uint8_t*>(W), ldw, M, N,
+                    K, e) != cudaSuccess)
+    return W4A8_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH;
 }
 
@@ -328,7 +334,9 @@ int gemm_w4(const int8_t* A, int64_t lda, const void* W, int64_t ldw, int M, int
   if (int rc = launch_w4(bn, cta, swap, tA, tW, p, grid, stream)) return rc;
   if (!splits) return W4A8_OK;
   const long long threads = (long long)M * ((N + 15) / 16);
-  w4a8_splitk_finish_kernel<<<unsigned((threads + 255) / 256), 256, 0, stream>>>(p);
+  if (launch_kernel(w4a8_splitk_finish_kernel, dim3(unsigned((threads + 255) / 256)), dim3(256), 0, stream, p) !=
+      cudaSuccess)
+    return W4A8_ERR_LAUNCH;
   return cudaGetLastError() == cudaSuccess ? W4A8_OK : W4A8_ERR_LAUNCH;
 }
 

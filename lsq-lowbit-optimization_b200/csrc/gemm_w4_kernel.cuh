@@ -137,6 +137,7 @@ __global__ void __launch_bounds__(kW4Threads, 1)
   uint8_t* base = smem_raw + (base_u32 - smem_u32(smem_raw));
   const uint32_t Sa = uint32_t(p.stages), Sp = uint32_t(p.pk_stages), Sb = uint32_t(p.b8_stages);
 
+  pdl_trigger();  // the next kernel of the stream may launch; it waits for this one in its own pdl_wait
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < Sa; ++s) { mbar_init(&full_a[s], 1); mbar_init(&empty_a[s], 1); }
     for (uint32_t s = 0; s < Sp; ++s) { mbar_init(&full_p[s], 1); mbar_init(&empty_p[s], W4Roles::kGroupWarps); }
@@ -170,6 +171,7 @@ __global__ void __launch_bounds__(kW4Threads, 1)
   if constexpr (kPair) cluster_sync();  // the peer's barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
+  pdl_wait();  // global memory only after the previous kernel of the stream has completed
   const int total_tiles = p.tiles_m * p.tiles_n * p.k_splits;  // work units
 
   if (warp == 0 || warp == 2) {
@@ -380,6 +382,8 @@ __global__ void __launch_bounds__(kW4Threads, 1)
 // Split-K finish: the fused epilogue over the int32 sums; one thread per
 // (row, 16 columns).
 __global__ void __launch_bounds__(256) w4a8_splitk_finish_kernel(const __grid_constant__ KParams p) {
+  pdl_trigger();
+  pdl_wait();
   const int chunks = (p.N + 15) / 16;
   const long long idx = blockIdx.x * 256LL + threadIdx.x;
   if (idx >= (long long)p.M * chunks) return;

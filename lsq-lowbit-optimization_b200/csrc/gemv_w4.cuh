@@ -43,6 +43,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32) w4a8_gemv_w4_kernel(const int
                                                                        int M, int N, int K,
                                                                        const __grid_constant__ EpiParams e) {
   extern __shared__ __align__(16) uint32_t gsm[];
+  pdl_trigger();
+  pdl_wait();
   const int t0 = int(blockIdx.y) * MT;  // this block's first token
   X += (long long)t0 * ldx;
   M = min(M - t0, MT);
@@ -147,6 +149,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32) w4a8_gemv_w4_rows_kernel(cons
                                                                        int M, int N, int K,
                                                                        const __grid_constant__ EpiParams e) {
   extern __shared__ __align__(16) uint32_t gsm[];
+  pdl_trigger();
+  pdl_wait();
   const int kw = K / 4;  // de-interleaved words per token
   uint32_t* xs = gsm;
   int* fin = reinterpret_cast<int*>(xs + MT * kw);

@@ -831,6 +831,7 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
   const uint32_t base_u32 = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* base = smem_raw + (base_u32 - smem_u32(smem_raw));
 
+  pdl_trigger();  // the next kernel of the stream may launch; it waits for this one in its own pdl_wait
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&bar_full[s], 1);
@@ -876,6 +877,10 @@ __global__ void __launch_bounds__(Roles<kConv>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_slot;
+  // Everything above touched only shared memory, TMEM and the tensor maps;
+  // global memory (weights included: a kernel ahead may have written them)
+  // is read and written only after the previous kernel has completed.
+  pdl_wait();
 
   const int total_tiles = p.tiles_m * p.tiles_n;
   const int kbpg = kConv ? p.conv.kb_per_group : p.num_kb;

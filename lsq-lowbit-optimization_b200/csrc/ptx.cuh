@@ -10,6 +10,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include "launch.cuh"
+
 namespace w4a8 {
 
 // ---------------------------------------------------------------------------
