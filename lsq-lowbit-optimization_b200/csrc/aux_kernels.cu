@@ -310,10 +310,21 @@ __global__ void avgpool_q_kernel(const float* __restrict__ x, int8_t* __restrict
     const int img = int(i / c);
     const float* xi = x + (long long)img * hw * c + ch;
     float s = 0.0f;
-    // Unrolled so that several pixels' loads are in flight; the adds keep
-    // their order (pixel 0, 1, 2, ...).
+    if (hw == 49) {
+      // 7 x 7 (the ResNet head), fully unrolled: more loads in flight per
+      // thread (12.3 -> 10.0 us at batch 256, 512 channels). The adds keep
+      // their order (pixel 0, 1, 2, ...).
+      float v[49];
+#pragma unroll
+      for (int p = 0; p < 49; ++p) v[p] = __ldg(xi + (long long)p * c);
+#pragma unroll
+      for (int p = 0; p < 49; ++p) s = __fadd_rn(s, v[p]);
+    } else {
+      // Unrolled so that several pixels' loads are in flight; the adds keep
+      // their order (pixel 0, 1, 2, ...).
 #pragma unroll 8
-    for (int p = 0; p < hw; ++p) s = __fadd_rn(s, __ldg(xi + (long long)p * c));
+      for (int p = 0; p < hw; ++p) s = __fadd_rn(s, __ldg(xi + (long long)p * c));
+    }
     const float mean = __fdiv_rn(s, float(hw));
     q[(long long)img * ldq + ch] = int8_t(quant1(mean, scale, qn, qp));
   }
