@@ -124,7 +124,7 @@ def test_resnet18_bs256_vs_converted_model_forward(cuda, resnet18_bs256):
     code step at the classifier input moves a logit by about 1e-2 of the
     largest logit, so the max-abs relative error is about 8e-3 whatever the
     kernels do (measured per source on a B200). The gates are therefore
-    top-1 agreement >= 99.9% (north_star's), the mean absolute error over
+    top-1 agreement >= 99.9% (the parity gate of this path), the mean absolute error over
     the largest logit <= 1e-3, and the max-abs relative error <= 2e-2."""
     import copy
 
