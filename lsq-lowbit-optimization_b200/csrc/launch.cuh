@@ -47,8 +47,9 @@ cudaError_t launch_kernel_attrs(void (*kern)(Exp...), dim3 grid, dim3 block, siz
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[4];
+  if (n_extra < 0 || n_extra > 3) return cudaErrorInvalidValue;
   int n = 0;
-  for (int i = 0; i < n_extra && n < 3; ++i) attr[n++] = extra[i];
+  for (int i = 0; i < n_extra; ++i) attr[n++] = extra[i];
   if (pdl_enabled()) {
     attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[n].val.programmaticStreamSerializationAllowed = 1;
