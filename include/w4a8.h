@@ -6,6 +6,10 @@
  * Nothing here allocates device memory; callers own every buffer. All calls
  * are asynchronous with respect to the host (kernels are enqueued on
  * `stream`), except w4a8_device_error which synchronises the device.
+ * Kernels are launched with programmatic dependent launch: one may start
+ * while the kernel ahead of it in `stream` finishes, and it waits for that
+ * kernel to complete before it reads or writes global memory, so stream
+ * order holds. W4A8_PDL=0 in the environment launches in plain stream order.
  *
  * Reference interfaces replaced (peihengzju/lsq-lowbit-optimization):
  *   csrc/int4_int8_ext.cpp:205-212   the six pybind ops of `int4_int8_ext`
